@@ -1,0 +1,73 @@
+// C++ entry points behind the C ABI, with the reference's namespace API
+// (src/rdna/fa2_forward_f16.hpp:10-44, src/rdna/fa2_forward_int8qk.hpp:10-46)
+// so code written against rdna::forwardF16 / rdna::forwardInt8QK links
+// against librdnattention.so unchanged.
+#pragma once
+
+#include <cstdint>
+
+namespace rdna {
+
+/// Q/K/V/output point at fp16, head_dim contiguous; strides in elements.
+/// rot_cos/rot_sin (if hasRope): fp32 [max(seqLen, keySeqLen), headDim/2].
+struct ForwardParams {
+    const void* q = nullptr;
+    const void* k = nullptr;
+    const void* v = nullptr;
+    void* o = nullptr;
+    const void* rot_cos = nullptr;
+    const void* rot_sin = nullptr;
+    int64_t qStrideB = 0, qStrideH = 0, qStrideS = 0;
+    int64_t kStrideB = 0, kStrideH = 0, kStrideS = 0;
+    int64_t vStrideB = 0, vStrideH = 0, vStrideS = 0;
+    int64_t oStrideB = 0, oStrideH = 0, oStrideS = 0;
+    uint32_t batchSize = 0;
+    uint32_t numHeads = 0;
+    uint32_t numKvHeads = 0;
+    uint32_t seqLen = 0;
+    uint32_t keySeqLen = 0;
+    uint32_t headDim = 0;  // multiple of 32 in [32, 512]
+    float scale = 1.0f;
+    uint32_t causal = 0;
+    uint32_t hasRope = 0;
+    int32_t windowSize = -1;  // <= 0: full attention
+};
+
+/// Q/K/V int8, head_dim contiguous; output fp16.
+struct ForwardParamsInt8QK {
+    const void* q = nullptr;
+    const void* k = nullptr;
+    const void* v = nullptr;
+    void* o = nullptr;
+    int64_t qStrideB = 0, qStrideH = 0, qStrideS = 0;
+    int64_t kStrideB = 0, kStrideH = 0, kStrideS = 0;
+    int64_t vStrideB = 0, vStrideH = 0, vStrideS = 0;
+    int64_t oStrideB = 0, oStrideH = 0, oStrideS = 0;
+    uint32_t batchSize = 0;
+    uint32_t numHeads = 0;
+    uint32_t numKvHeads = 0;
+    uint32_t seqLen = 0;
+    uint32_t keySeqLen = 0;
+    uint32_t headDim = 0;  // 64 or 128
+    float scale = 1.0f;
+    float qScale = 1.0f;
+    float kScale = 1.0f;
+    float vScale = 1.0f;
+    uint32_t causal = 0;
+    int32_t windowSize = -1;
+    const void* qScaleVec = nullptr;  // const float*, (batch, heads, seq)
+    const void* kScaleVec = nullptr;  // const float*, (batch, kv_heads, key_seq)
+};
+
+/// Enqueues the FP16 forward on `stream` (a cudaStream_t). Non-blocking. 0 on success.
+int forwardF16(const ForwardParams& params, void* stream);
+/// Reason the most recent forwardF16() call on this thread failed, or nullptr.
+const char* lastError();
+/// Enqueues the INT8 forward on `stream`. Non-blocking. 0 on success.
+int forwardInt8QK(const ForwardParamsInt8QK& params, void* stream);
+/// Reason the most recent forwardInt8QK() call on this thread failed, or nullptr.
+const char* lastErrorInt8QK();
+/// Whether a CUDA device is visible.
+bool hasDevice();
+
+}  // namespace rdna

@@ -1,0 +1,90 @@
+/*
+ * rdnattention for B200 (sm_100a) — stable C ABI of librdnattention.so.
+ *
+ * Drop-in replacement for the reference library's C ABI
+ * (src/c_api.hpp:16-87 of dmonkman/RDNAttention): identical symbol names,
+ * argument order, argument meaning and return codes, so the reference's own
+ * ctypes binding (rdnattention/__init__.py:94-130) loads this library
+ * unchanged.  Device pointers are CUDA device pointers and `stream` is a
+ * cudaStream_t (the reference's hipStream_t slot).
+ *
+ * Every function operates on caller-owned device memory; the library keeps
+ * no handle table and allocates no device memory.  Launches are enqueued on
+ * `stream` and never block the host.
+ */
+#ifndef RDNATTENTION_H_
+#define RDNATTENTION_H_
+
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define RDNA_API_EXPORT __declspec(dllexport)
+#else
+#define RDNA_API_EXPORT __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+#define RDNA_API extern "C" RDNA_API_EXPORT
+#else
+#define RDNA_API RDNA_API_EXPORT
+#endif
+
+/* 1 if at least one CUDA device is visible, else 0.
+ * Replaces src/c_api.hpp:16 (rdna_has_device). */
+RDNA_API int32_t rdna_has_device(void);
+
+/* Reason the most recent failing call on this thread failed ("" if none
+ * has).  Thread-local, never cleared by a successful call.
+ * Replaces src/c_api.hpp:18-19 (rdna_get_error). */
+RDNA_API const char* rdna_get_error(void);
+
+/* FP16 forward attention.  q/k/v/output: fp16, head_dim contiguous, strides
+ * in ELEMENTS for the batch/head/seq axes.  head_dim: any multiple of 32 in
+ * [32, 512].  rot_cos/rot_sin (read when has_rope != 0): fp32
+ * [max(seq_len, key_seq_len), head_dim/2], contiguous, interleaved-pair RoPE
+ * applied to Q and K in-kernel.  num_kv_heads < num_heads selects GQA
+ * (num_heads % num_kv_heads == 0).  causal != 0 aligns the causal diagonal
+ * to the end of the key sequence; window_size > 0 limits each query to a
+ * one-sided (causal) or two-sided (|q+delta-k| <= window_size/2) band.
+ * Returns 0, or -3 with rdna_get_error() set.
+ * Replaces src/c_api.hpp:36-57 (rdna_attention_forward). */
+RDNA_API int32_t rdna_attention_forward(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* stream);
+
+/* INT8 forward attention (both GEMMs in int8, s32 accumulation), fp16
+ * output.  head_dim 64 or 128; causal, window, GQA; no RoPE.  Dequant:
+ * S = float(q.k) * q_scale_i * k_scale_j * scale; q_scale_vec (B, H, S) /
+ * k_scale_vec (B, Hkv, KS) fp32 per-token scales override q_scale / k_scale
+ * when non-NULL; v_scale is per-tensor.  P is quantised min(127,
+ * lround(p * 127)).  Returns 0, or -3 with rdna_get_error() set.
+ * Replaces src/c_api.hpp:64-87 (rdna_attention_forward_int8qk). */
+RDNA_API int32_t rdna_attention_forward_int8qk(
+    const void* q, const void* k, const void* v, void* output,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, float q_scale, float k_scale, float v_scale,
+    const void* q_scale_vec, const void* k_scale_vec,
+    int32_t causal, int32_t window_size, void* stream);
+
+/* ---- Extensions beyond the reference ABI (no counterpart there) ---- */
+
+/* Reads and clears the device status word of the current device: out[0] =
+ * first error code a kernel recorded (a bounded wait that expired), out[1] =
+ * number of such events.  Synchronises the current device.  Returns 0, or
+ * -3 with rdna_get_error() set. */
+RDNA_API int32_t rdna_debug_read_status(int32_t* out2);
+
+#endif /* RDNATTENTION_H_ */

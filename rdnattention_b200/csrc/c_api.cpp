@@ -1,0 +1,139 @@
+// extern "C" exports of librdnattention.so (include/rdnattention.h).  Same
+// marshalling and error contract as the reference (src/c_api.cpp:1-195):
+// arguments are copied into the rdna:: parameter structs, a failure returns
+// -3 and leaves a thread-local message that is never cleared on success.
+// RDNA_API is on the definitions as well as the declarations, so a
+// definition whose signature drifts from the header fails to compile.
+#include "rdnattention.h"
+
+#include <array>
+#include <cstdio>
+
+#include "rdna/forward.hpp"
+
+namespace rdna {
+int debugReadStatus(int32_t* out2, const char** why);
+}
+
+namespace {
+
+thread_local std::array<char, 512> g_error{};
+
+void set_error(const char* fmt, const char* detail) {
+    std::snprintf(g_error.data(), g_error.size(), fmt, detail != nullptr ? detail : "unknown error");
+}
+
+}  // namespace
+
+RDNA_API int32_t rdna_has_device(void) { return rdna::hasDevice() ? 1 : 0; }
+
+RDNA_API const char* rdna_get_error(void) { return g_error.data(); }
+
+RDNA_API int32_t rdna_attention_forward(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* stream) {
+    rdna::ForwardParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = output;
+    p.rot_cos = rot_cos;
+    p.rot_sin = rot_sin;
+    p.qStrideB = q_stride_b;
+    p.qStrideH = q_stride_h;
+    p.qStrideS = q_stride_s;
+    p.kStrideB = k_stride_b;
+    p.kStrideH = k_stride_h;
+    p.kStrideS = k_stride_s;
+    p.vStrideB = v_stride_b;
+    p.vStrideH = v_stride_h;
+    p.vStrideS = v_stride_s;
+    p.oStrideB = o_stride_b;
+    p.oStrideH = o_stride_h;
+    p.oStrideS = o_stride_s;
+    p.batchSize = batch_size;
+    p.numHeads = num_heads;
+    p.numKvHeads = num_kv_heads;
+    p.seqLen = seq_len;
+    p.keySeqLen = key_seq_len;
+    p.headDim = head_dim;
+    p.scale = scale;
+    p.causal = causal != 0 ? 1u : 0u;
+    p.hasRope = has_rope != 0 ? 1u : 0u;
+    p.windowSize = window_size;
+    if (rdna::forwardF16(p, stream) != 0) {
+        set_error("Attention (fp16) failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API int32_t rdna_attention_forward_int8qk(
+    const void* q, const void* k, const void* v, void* output,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, float q_scale, float k_scale, float v_scale,
+    const void* q_scale_vec, const void* k_scale_vec,
+    int32_t causal, int32_t window_size, void* stream) {
+    rdna::ForwardParamsInt8QK p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = output;
+    p.qStrideB = q_stride_b;
+    p.qStrideH = q_stride_h;
+    p.qStrideS = q_stride_s;
+    p.kStrideB = k_stride_b;
+    p.kStrideH = k_stride_h;
+    p.kStrideS = k_stride_s;
+    p.vStrideB = v_stride_b;
+    p.vStrideH = v_stride_h;
+    p.vStrideS = v_stride_s;
+    p.oStrideB = o_stride_b;
+    p.oStrideH = o_stride_h;
+    p.oStrideS = o_stride_s;
+    p.batchSize = batch_size;
+    p.numHeads = num_heads;
+    p.numKvHeads = num_kv_heads;
+    p.seqLen = seq_len;
+    p.keySeqLen = key_seq_len;
+    p.headDim = head_dim;
+    p.scale = scale;
+    p.qScale = q_scale;
+    p.kScale = k_scale;
+    p.vScale = v_scale;
+    p.causal = causal != 0 ? 1u : 0u;
+    p.windowSize = window_size;
+    p.qScaleVec = q_scale_vec;
+    p.kScaleVec = k_scale_vec;
+    if (rdna::forwardInt8QK(p, stream) != 0) {
+        set_error("Attention (int8qk) failed: %s", rdna::lastErrorInt8QK());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API int32_t rdna_debug_read_status(int32_t* out2) {
+    const char* why = nullptr;
+    if (out2 == nullptr) {
+        set_error("Debug status failed: %s", "null output pointer");
+        return -3;
+    }
+    if (rdna::debugReadStatus(out2, &why) != 0) {
+        set_error("Debug status failed: %s", why);
+        return -3;
+    }
+    return 0;
+}

@@ -1,0 +1,869 @@
+// FlashAttention-2 forward for sm_100a: TMA -> shared memory, tcgen05.mma
+// into TMEM, warp-specialised online softmax.
+//
+// One CTA owns NT (1 or 2) query tiles of 128 rows that share a KV head:
+//   * NT = 2, pair_heads: two query heads of one GQA group, same rows, so
+//     every K/V tile loaded into shared memory feeds two MMAs;
+//   * NT = 2, row pairs: two consecutive 128-row blocks of one head (odd G);
+//   * NT = 1: one tile (head_dim > 128, where TMEM holds a single O tile).
+//
+// Warp roles (THREADS = 128 * NT + 128):
+//   warps [0, 4*NT)   softmax warpgroup t = warp / 4; thread = query row =
+//                     TMEM lane.  Loads S from TMEM, masks boundary blocks,
+//                     keeps the running max / row sum, writes P (fp16 or
+//                     int8) back over S in TMEM, rescales O in TMEM when
+//                     needed, and runs the epilogue (O / l -> fp16 -> TMA store).
+//   warp 4*NT         TMA producer (one lane): Q tiles once, then a ring of
+//                     K tiles and a ring of V tiles.
+//   warp 4*NT+1       MMA issuer (one lane): S_t = Q_t K^T (SS form),
+//                     O_t += P_t V (TS form, P read from TMEM).  Per block j
+//                     it issues, for each tile, PV(j) then QK(j+1), so one
+//                     tile's softmax overlaps the other tile's MMAs.
+//   warps 4*NT+2..+3  RoPE: rotate Q tiles once and every K tile in shared
+//                     memory (interleaved pairs) before the MMA reads them.
+//
+// TMEM columns: S_t at [t*BC, t*BC+BC) (P aliases its first columns);
+// FP16: O_t (fp32) after all S.  INT8: ACC_t (s32 PV accumulator) then
+// O_t (fp32, flushed from ACC whenever the row max moves).
+//
+// Semantics follow the reference kernel (src/rdna/fa2_forward_f16.hip:633-741,
+// src/rdna/fa2_forward_int8qk.hip:229-495): exp2-domain online softmax with
+// scale*log2(e), P rounded to fp16 (or quantised min(127, lround(p*127)) for
+// INT8) while the row sum uses the unrounded p, rows with no visible key
+// produce 0, masks per src/rdna/fa2_forward_f16.hip:297-348.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "sm100.cuh"
+
+namespace rdna {
+namespace prefill {
+
+using namespace sm100;
+
+constexpr int BM = 128;  // query rows per tile (= TMEM lanes)
+
+struct Params {
+    int B, H, Hkv, S, KS;
+    int G;        // H / Hkv
+    int delta;    // KS - S
+    int causal;
+    int window;   // <= 0: no window
+    int has_rope;
+    int pair_heads;
+    int n_rb;     // ceil(S / BM)
+    int n_rp;     // ceil(n_rb / 2)
+    int n_split;  // output column slices per tile (head_dim > 256)
+    int dv_split; // output columns per slice (multiple of the box width)
+    float scale_log2;
+    const float* rot_cos;
+    const float* rot_sin;
+    // INT8 path
+    float q_scale, k_scale, pv_scale;
+    const float* q_vec;
+    const float* k_vec;
+};
+
+template <int D_, int DVMAX_, int BC_, int NT_, int NSK_, int NSV_, bool I8_>
+struct Traits {
+    static constexpr int D = D_;          // QK depth (head_dim)
+    static constexpr int DVMAX = DVMAX_;  // output columns per CTA (<= 256)
+    static constexpr int BC = BC_;        // keys per block
+    static constexpr int NT = NT_;
+    static constexpr int NSK = NSK_;
+    static constexpr int NSV = NSV_;
+    static constexpr bool I8 = I8_;
+    static constexpr int ESZ = I8 ? 1 : 2;
+    static constexpr int ROW_BYTES = D * ESZ;
+    static constexpr int SW = (ROW_BYTES % 128 == 0) ? 128 : 64;  // swizzle span (bytes)
+    static constexpr uint32_t LAYOUT = (SW == 128) ? 2u : 4u;    // UMMA layout code
+    static constexpr int BOX = SW / ESZ;                          // elements per box row
+    static constexpr int NBOX = D / BOX;
+    static constexpr int NBOX_V = DVMAX / BOX;
+    static constexpr int KSTEP = I8 ? 32 : 16;  // MMA K per instruction (elements)
+    static constexpr int STEPS_PER_BOX = SW / 32;
+    static constexpr int Q_BOX_BYTES = BM * SW;
+    static constexpr int K_BOX_BYTES = BC * SW;
+    static constexpr int Q_TILE = NBOX * Q_BOX_BYTES;
+    static constexpr int K_TILE = NBOX * K_BOX_BYTES;
+    static constexpr int V_TILE = NBOX_V * K_BOX_BYTES;
+    static constexpr int THREADS = 128 * NT + 128;
+    static constexpr int WARP_PROD = 4 * NT;
+    static constexpr int WARP_MMA = 4 * NT + 1;
+    static constexpr int WARP_ROPE0 = 4 * NT + 2;
+
+    // TMEM columns
+    static constexpr int S_COL0 = 0;
+    static constexpr int ACC_COL0 = NT * BC;                         // INT8 only
+    static constexpr int O_COL0 = I8 ? NT * BC + NT * DVMAX : NT * BC;
+    static constexpr int TMEM_USED = O_COL0 + NT * DVMAX;
+    static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
+                                     : TMEM_USED <= 256 ? 256 : 512;
+    static_assert(TMEM_USED <= 512, "TMEM budget");
+    static_assert(D % BOX == 0 && DVMAX % BOX == 0, "head_dim must tile into boxes");
+    static_assert(BC % KSTEP == 0 && BC % 32 == 0, "key block");
+
+    // Output (fp16) staging geometry.  FP16: O uses Q's swizzle and box and is
+    // staged in Q_t's buffer.  INT8: fp16 rows are twice as wide as the int8
+    // Q rows, so O gets its own 128B-swizzled staging region.
+    static constexpr int O_SW = I8 ? 128 : SW;
+    static constexpr int O_BOX = O_SW / 2;
+    static constexpr int O_BOX_BYTES = BM * O_SW;
+    static constexpr int O_TILE = (DVMAX / O_BOX) * O_BOX_BYTES;
+    static_assert(DVMAX % O_BOX == 0, "output slice tiles into boxes");
+
+    // Shared memory: [misc 1 KB (+ INT8 key scales)][Q tiles][K ring][V ring]
+    // (+ INT8 O staging), tiles 1024-aligned.
+    static constexpr int MISC_BYTES = 1024 + (I8 ? NT * 2 * BC * 4 : 0);
+    static constexpr int OFF_Q = ((MISC_BYTES + 1023) / 1024) * 1024;
+    static constexpr int OFF_K = OFF_Q + NT * Q_TILE;
+    static constexpr int OFF_V = OFF_K + NSK * K_TILE;
+    static constexpr int OFF_O = I8 ? OFF_V + NSV * V_TILE : OFF_Q;
+    static constexpr int O_STRIDE = I8 ? O_TILE : Q_TILE;  // staging bytes between tiles
+    static constexpr int SMEM_BYTES = OFF_V + NSV * V_TILE + (I8 ? NT * O_TILE : 0) + 1024;  // + align slack
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+    static_assert(I8 || O_TILE <= Q_TILE, "O staging fits in the Q tile");
+
+    static constexpr uint32_t IDESC_QK = instr_desc(I8 ? 2u : 1u, I8 ? 1u : 0u, 0u, BM, BC);
+    static constexpr float THRESH = I8 ? 0.0f : 8.0f;  // log2-domain slack before O is rescaled
+};
+
+// Barrier slots inside the misc region.
+struct Bars {
+    static constexpr int Q_FULL = 0, Q_READY = 1, DRAIN = 2;
+    static constexpr int K_FULL = 4;      // +NSK
+    static constexpr int K_READY = 12;    // +NSK
+    static constexpr int K_EMPTY = 20;    // +NSK
+    static constexpr int V_FULL = 28;     // +NSV
+    static constexpr int V_EMPTY = 36;    // +NSV
+    static constexpr int S_FULL = 44;     // +NT
+    static constexpr int P_FULL = 46;     // +NT
+    static constexpr int O_FULL = 48;     // +NT
+    static constexpr int KS_FULL = 50;    // +2*NT (INT8 per-key scale handoff, by block parity)
+    static constexpr int EPI = 54;        // +NT (O staging written)
+    static constexpr int COUNT = 56;
+    static constexpr int TMEM_SLOT = COUNT * 8;      // u32 TMEM base
+    static constexpr int ABORT_SLOT = COUNT * 8 + 4; // int abort flag
+};
+
+// Error sites recorded in the status word (debug aid).
+enum Site : int {
+    SITE_PROD_KEMPTY = 0x101, SITE_PROD_VEMPTY = 0x102,
+    SITE_MMA_Q = 0x201, SITE_MMA_K = 0x202, SITE_MMA_V = 0x203, SITE_MMA_P = 0x204,
+    SITE_SM_S = 0x301, SITE_SM_O = 0x302, SITE_SM_Q = 0x303, SITE_SM_KS = 0x304, SITE_SM_EPI = 0x305,
+    SITE_ROPE_Q = 0x401, SITE_ROPE_K = 0x402,
+};
+
+struct Work {
+    int b, kvh;
+    int head[2];
+    int row0[2];
+    bool valid[2];
+    int split;
+};
+
+template <class T>
+__device__ __forceinline__ Work decode_work(const Params& p, int item) {
+    Work w;
+    w.split = item % p.n_split;
+    item /= p.n_split;
+    if constexpr (T::NT == 1) {
+        const int per = p.B * p.H;
+        const int rb = p.n_rb - 1 - item / per;  // longest causal rows first
+        const int rem = item % per;
+        w.b = rem / p.H;
+        const int h = rem % p.H;
+        w.kvh = h / p.G;
+        w.head[0] = w.head[1] = h;
+        w.row0[0] = rb * BM;
+        w.row0[1] = 0;
+        w.valid[0] = true;
+        w.valid[1] = false;
+    } else if (p.pair_heads) {
+        const int np = p.G / 2;
+        const int per = p.B * p.Hkv * np;
+        const int rb = p.n_rb - 1 - item / per;
+        int rem = item % per;
+        w.b = rem / (p.Hkv * np);
+        rem %= p.Hkv * np;
+        w.kvh = rem / np;
+        const int hp = rem % np;
+        w.head[0] = w.kvh * p.G + 2 * hp;
+        w.head[1] = w.head[0] + 1;
+        w.row0[0] = w.row0[1] = rb * BM;
+        w.valid[0] = w.valid[1] = true;
+    } else {
+        const int per = p.B * p.H;
+        const int rp = p.n_rp - 1 - item / per;
+        const int rem = item % per;
+        w.b = rem / p.H;
+        const int h = rem % p.H;
+        w.kvh = h / p.G;
+        w.head[0] = w.head[1] = h;
+        w.row0[0] = 2 * rp * BM;
+        w.row0[1] = (2 * rp + 1) * BM;
+        w.valid[0] = true;
+        w.valid[1] = w.row0[1] < p.S;
+    }
+    return w;
+}
+
+// Visible key interval of query row q (clamped to [0, KS-1]); empty if lo > hi.
+__device__ __forceinline__ void row_keys(const Params& p, int q, int& lo, int& hi) {
+    lo = 0;
+    hi = p.KS - 1;
+    const int qd = q + p.delta;
+    if (p.causal) hi = min(hi, qd);
+    if (p.window > 0) {
+        if (p.causal) {
+            lo = max(lo, qd - p.window + 1);
+        } else {
+            const int half = p.window / 2;
+            lo = max(lo, qd - half);
+            hi = min(hi, qd + half);
+        }
+    }
+}
+
+// [a, e) range of key blocks tile rows [row0, row0+BM) can touch.
+template <class T>
+__device__ __forceinline__ void tile_blocks(const Params& p, int row0, bool valid, int& a, int& e) {
+    a = e = 0;
+    if (!valid) return;
+    const int rlast = min(row0 + BM - 1, p.S - 1);
+    int lo0, hi0, lo1, hi1;
+    row_keys(p, row0, lo0, hi0);
+    row_keys(p, rlast, lo1, hi1);
+    const int lo = lo0, hi = hi1;
+    if (lo > hi || hi < 0 || lo > p.KS - 1) return;
+    a = lo / T::BC;
+    e = hi / T::BC + 1;
+}
+
+// Whether block j needs no per-element mask for any row of the tile.
+template <class T>
+__device__ __forceinline__ bool block_full(const Params& p, int row0, int j) {
+    int loA, hiA, loB, hiB;
+    row_keys(p, row0, loA, hiA);           // smallest hi
+    row_keys(p, row0 + BM - 1, loB, hiB);  // largest lo
+    const int k0 = j * T::BC, k1 = j * T::BC + T::BC - 1;
+    return k0 >= loB && k1 <= hiA;
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` inside one swizzled box.
+template <int SW>
+__device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
+    const uint32_t off = static_cast<uint32_t>(row * SW + chunk * 16);
+    return off ^ (((off >> 7) & (SW / 16 - 1)) << 4);
+}
+
+// --------------------------------------------------------------- softmax
+template <class T>
+__device__ __forceinline__ void load_s_row(uint32_t taddr, uint32_t* r) {
+    if constexpr (T::BC == 128) {
+        tmem_ld_x128(taddr, r);
+    } else if constexpr (T::BC == 64) {
+        tmem_ld_x64(taddr, r);
+    } else {
+        tmem_ld_x32(taddr, r);
+    }
+}
+
+// lround(x) for x >= 0, exactly (round half away from zero).
+__device__ __forceinline__ int lround_pos(float x) {
+    const float t = truncf(x);
+    return static_cast<int>(t) + ((x - t) >= 0.5f ? 1 : 0);
+}
+
+// Warp-uniform bounded wait: every lane of the warp gets the same answer, so
+// the warp-collective tcgen05.ld/st that follow never diverge.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const Abort& ab, int site) {
+    bool ok = mbar_wait(bar, parity, ab, site);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Softmax warpgroup for tile t.  Loops never exit early and no named
+// barriers are used: after an abort every remaining wait returns false at
+// once and the work is skipped, so all threads reach the kernel's final
+// __syncthreads.
+template <class T>
+__device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work& w, int t, uint8_t* smem,
+                             uint32_t tmem, const Abort& ab, int dv, int dv0) {
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int wq = warp % 4;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_base + T::S_COL0 + t * T::BC;
+    const uint32_t tO = tmem + lane_base + T::O_COL0 + t * T::DVMAX;
+    const uint32_t tACC = tmem + lane_base + T::ACC_COL0 + t * T::DVMAX;
+    const uint32_t bars = smem_u32(smem);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+
+    if (!w.valid[t]) return;  // uniform for the warpgroup
+    const int row0 = w.row0[t];
+    const int q = row0 + r;
+    int a, e;
+    tile_blocks<T>(p, row0, w.valid[t], a, e);
+    int klo, khi;
+    row_keys(p, q, klo, khi);
+
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY;
+    float l = 0.f;
+    bool aborted = false;
+
+    // INT8 state
+    float rowscale = 1.f;
+    bool oflushed = false;
+    int since_flush = 0;
+    float* ksbuf = nullptr;
+    const bool kvec = T::I8 && p.k_vec != nullptr;
+    if constexpr (T::I8) {
+        float qs = p.q_scale;
+        if (p.q_vec != nullptr && q < p.S) qs = p.q_vec[(static_cast<int64_t>(w.b) * p.H + w.head[t]) * p.S + q];
+        rowscale = qs * sl2;
+        if (!kvec) rowscale *= p.k_scale;
+        ksbuf = reinterpret_cast<float*>(smem + 1024) + t * 2 * T::BC;
+    }
+
+    int it = 0;
+    for (int j = a; j < e; ++j, ++it) {
+        if constexpr (T::I8) {
+            if (kvec) {
+                // stage this block's per-key scales; buffer (it & 1) is reused every second block
+                const int buf = it & 1;
+                if (r < T::BC) {
+                    const int key = j * T::BC + r;
+                    ksbuf[buf * T::BC + r] =
+                        key < p.KS ? p.k_vec[(static_cast<int64_t>(w.b) * p.Hkv + w.kvh) * p.KS + key] : 0.f;
+                }
+                mbar_arrive(bar(Bars::KS_FULL + 2 * t + buf));
+                if (!aborted && !warp_wait(bar(Bars::KS_FULL + 2 * t + buf), (it >> 1) & 1, ab, SITE_SM_KS))
+                    aborted = true;
+            }
+        }
+        if (!aborted && !warp_wait(bar(Bars::S_FULL + t), it & 1, ab, SITE_SM_S)) aborted = true;
+        if (aborted) continue;
+        tc_fence_after();
+
+        uint32_t raw[T::BC];
+        load_s_row<T>(tS, raw);
+        float* x = reinterpret_cast<float*>(raw);
+        const bool full = block_full<T>(p, row0, j);
+        const int lo = klo - j * T::BC, hi = khi - j * T::BC;
+
+        float mx = -INFINITY;
+        if constexpr (T::I8) {
+            const float* ksb = ksbuf + (it & 1) * T::BC;
+#pragma unroll
+            for (int c = 0; c < T::BC; ++c) {
+                float v = static_cast<float>(static_cast<int>(raw[c])) * rowscale;
+                if (kvec) v *= ksb[c];
+                x[c] = v;
+            }
+            if (!full) {
+#pragma unroll
+                for (int c = 0; c < T::BC; ++c)
+                    if (c < lo || c > hi) x[c] = -INFINITY;
+            }
+#pragma unroll
+            for (int c = 0; c < T::BC; ++c) mx = fmaxf(mx, x[c]);
+        } else {
+            if (sl2 > 0.f) {
+                if (!full) {
+#pragma unroll
+                    for (int c = 0; c < T::BC; ++c)
+                        if (c < lo || c > hi) x[c] = -INFINITY;
+                }
+#pragma unroll
+                for (int c = 0; c < T::BC; ++c) mx = fmaxf(mx, x[c]);
+                mx *= sl2;
+            } else {
+                // non-positive scale: scale first, then mask (rare; keeps max semantics exact)
+#pragma unroll
+                for (int c = 0; c < T::BC; ++c) {
+                    float v = x[c] * sl2;
+                    if (!full && (c < lo || c > hi)) v = -INFINITY;
+                    x[c] = v;
+                    mx = fmaxf(mx, v);
+                }
+            }
+        }
+
+        const float m_new = fmaxf(m_ref, mx);
+        float corr = 1.f;
+        bool rescale = false;
+        if (m_new > m_ref + T::THRESH) {
+            corr = ex2(m_ref - m_new);  // 0 when m_ref = -inf
+            l *= corr;
+            rescale = (it > 0);
+            m_ref = m_new;
+        }
+
+        if constexpr (!T::I8) {
+            // O(tmem) *= corr.  PV(j-1) is complete: S_FULL(j) was committed after it.
+            if (__any_sync(0xffffffffu, rescale)) {
+                const float c = rescale ? corr : 1.f;
+                for (int c0 = 0; c0 < dv; c0 += 32) {
+                    uint32_t o[32];
+                    tmem_ld_x32(tO + c0, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * c);
+                    tmem_st_x32(tO + c0, o);
+                }
+                tmem_wait_st();
+            }
+        } else {
+            // INT8: the s32 accumulator holds sum(Pq * V) quantised against the current max;
+            // fold it into the fp32 O whenever the max moves (and every 512 blocks, bounding s32).
+            const bool flush = rescale || (it > 0 && since_flush >= 512);
+            if (__any_sync(0xffffffffu, flush)) {
+                const float c = rescale ? corr : 1.f;
+                for (int c0 = 0; c0 < dv; c0 += 32) {
+                    uint32_t acc[32], o[32];
+                    tmem_ld_x32(tACC + c0, acc);
+                    tmem_ld_x32(tO + c0, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float of = oflushed ? __uint_as_float(o[i]) : 0.f;
+                        const float nv = (of + static_cast<float>(static_cast<int>(acc[i])) * p.pv_scale) * c;
+                        o[i] = flush ? __float_as_uint(nv) : o[i];
+                        acc[i] = flush ? 0u : acc[i];
+                    }
+                    tmem_st_x32(tO + c0, o);
+                    tmem_st_x32(tACC + c0, acc);
+                }
+                tmem_wait_st();
+                if (flush) {
+                    oflushed = true;
+                    since_flush = 0;
+                }
+            }
+            ++since_flush;
+        }
+
+        // P = exp2(s*scale*log2e - m); the row sum uses the unrounded values
+        const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        float lsum = 0.f;
+        // P goes back over S in 32-key chunks (S is already in registers), so only
+        // one chunk of packed P is live at a time.
+        if constexpr (!T::I8) {
+            const float mul = (sl2 > 0.f) ? sl2 : 1.f;
+#pragma unroll
+            for (int c0 = 0; c0 < T::BC; c0 += 32) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int c = 0; c < 32; c += 2) {
+                    const float p0 = ex2(fmaf(x[c0 + c], mul, neg_m));
+                    const float p1 = ex2(fmaf(x[c0 + c + 1], mul, neg_m));
+                    lsum += p0 + p1;
+                    pk[c / 2] = pack_half2(p0, p1);
+                }
+                tmem_st_x16(tS + c0 / 2, pk);
+            }
+        } else {
+#pragma unroll
+            for (int c0 = 0; c0 < T::BC; c0 += 32) {
+                uint32_t pk[8];
+#pragma unroll
+                for (int c = 0; c < 32; c += 4) {
+                    uint32_t word = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float pv = ex2(x[c0 + c + i] + neg_m);
+                        lsum += pv;
+                        const int qv = min(127, lround_pos(pv * 127.f));
+                        word |= static_cast<uint32_t>(qv) << (8 * i);
+                    }
+                    pk[c / 4] = word;
+                }
+                tmem_st_x8(tS + c0 / 4, pk);
+            }
+        }
+        l += lsum;
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(Bars::P_FULL + t));
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    const bool has_blocks = e > a;
+    if (!aborted && has_blocks && !warp_wait(bar(Bars::O_FULL + t), 0, ab, SITE_SM_O)) aborted = true;
+    if (!aborted) tc_fence_after();
+    // FP16 stages O in Q_t's buffer: its TMA load (and RoPE) must have landed
+    if (!aborted && !T::I8 && !warp_wait(bar(p.has_rope ? Bars::Q_READY : Bars::Q_FULL), 0, ab, SITE_SM_Q))
+        aborted = true;
+
+    uint8_t* stage = smem + T::OFF_O + t * T::O_STRIDE;
+    if (!aborted) {
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        for (int c0 = 0; c0 < dv; c0 += 32) {
+            float o[32];
+            if (has_blocks) {
+                uint32_t ov[32];
+                tmem_ld_x32(tO + c0, ov);
+                if constexpr (T::I8) {
+                    uint32_t acc[32];
+                    tmem_ld_x32(tACC + c0, acc);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float of = oflushed ? __uint_as_float(ov[i]) : 0.f;
+                        o[i] = (of + static_cast<float>(static_cast<int>(acc[i])) * p.pv_scale) * inv;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(ov[i]) * inv;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[i] = 0.f;
+            }
+            // 32 fp16 = 4 chunks of 16 bytes
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                uint4 v;
+                v.x = pack_half2(o[8 * g + 0], o[8 * g + 1]);
+                v.y = pack_half2(o[8 * g + 2], o[8 * g + 3]);
+                v.z = pack_half2(o[8 * g + 4], o[8 * g + 5]);
+                v.w = pack_half2(o[8 * g + 6], o[8 * g + 7]);
+                const int col = c0 + 8 * g;
+                const int box = col / T::O_BOX;
+                const int chunk = (col % T::O_BOX) / 8;
+                *reinterpret_cast<uint4*>(stage + box * T::O_BOX_BYTES + swz_off<T::O_SW>(r, chunk)) = v;
+            }
+        }
+        fence_proxy_async_smem();
+    }
+    mbar_arrive(bar(Bars::EPI + t));
+    if (r == 0) {
+        if (!aborted && mbar_wait(bar(Bars::EPI + t), 0, ab, SITE_SM_EPI) && !*ab.flag) {
+            const int nbox = dv / T::O_BOX;
+            for (int bx = 0; bx < nbox; ++bx)
+                tma_store_4d(tmO, smem_u32(stage + bx * T::O_BOX_BYTES), dv0 + bx * T::O_BOX, row0, w.head[t], w.b);
+            bulk_commit();
+            bulk_wait_read_all();
+        }
+    }
+}
+
+// -------------------------------------------------------------- producer
+template <class T>
+__device__ void producer_role(const Params& p, const CUtensorMap* tmQ, const CUtensorMap* tmK,
+                              const CUtensorMap* tmV, const Work& w, int jlo, int jhi, uint8_t* smem,
+                              const Abort& ab, int dv, int dv0) {
+    const uint32_t bars = smem_u32(smem);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+    prefetch_tmap(tmQ);
+    prefetch_tmap(tmK);
+    prefetch_tmap(tmV);
+    const uint64_t pol_q = policy_evict_first();
+    const uint64_t pol_kv = policy_evict_last();
+
+    mbar_arrive_expect_tx(bar(Bars::Q_FULL), T::NT * T::Q_TILE);
+    for (int t = 0; t < T::NT; ++t) {
+        const uint32_t dst = smem_u32(smem + T::OFF_Q + t * T::Q_TILE);
+        for (int bx = 0; bx < T::NBOX; ++bx)
+            tma_load_4d(dst + bx * T::Q_BOX_BYTES, tmQ, bar(Bars::Q_FULL), bx * T::BOX, w.row0[t], w.head[t], w.b,
+                        pol_q);
+    }
+    const int nbox_v = dv / T::BOX;
+    int kfill[T::NSK] = {0};
+    int vfill[T::NSV] = {0};
+    bool ok = true;
+    int i = 0;
+    for (int j = jlo; j < jhi && ok; ++j, ++i) {
+        const int ks = i % T::NSK, kn = i / T::NSK;
+        if (!mbar_wait(bar(Bars::K_EMPTY + ks), (kn & 1) ^ 1, ab, SITE_PROD_KEMPTY)) {
+            ok = false;
+            break;
+        }
+        mbar_arrive_expect_tx(bar(Bars::K_FULL + ks), T::K_TILE);
+        const uint32_t kdst = smem_u32(smem + T::OFF_K + ks * T::K_TILE);
+        for (int bx = 0; bx < T::NBOX; ++bx)
+            tma_load_4d(kdst + bx * T::K_BOX_BYTES, tmK, bar(Bars::K_FULL + ks), bx * T::BOX, j * T::BC, w.kvh, w.b,
+                        pol_kv);
+        kfill[ks]++;
+        const int vs = i % T::NSV, vn = i / T::NSV;
+        if (!mbar_wait(bar(Bars::V_EMPTY + vs), (vn & 1) ^ 1, ab, SITE_PROD_VEMPTY)) {
+            ok = false;
+            break;
+        }
+        mbar_arrive_expect_tx(bar(Bars::V_FULL + vs), nbox_v * T::K_BOX_BYTES);
+        const uint32_t vdst = smem_u32(smem + T::OFF_V + vs * T::V_TILE);
+        for (int bx = 0; bx < nbox_v; ++bx)
+            tma_load_4d(vdst + bx * T::K_BOX_BYTES, tmV, bar(Bars::V_FULL + vs), dv0 + bx * T::BOX, j * T::BC, w.kvh,
+                        w.b, pol_kv);
+        vfill[vs]++;
+    }
+    if (!ok) {
+        // unwind: let every issued copy land before the CTA can exit
+        mbar_wait_drain(bar(Bars::Q_FULL), 0);
+        for (int s = 0; s < T::NSK; ++s)
+            if (kfill[s] > 0) mbar_wait_drain(bar(Bars::K_FULL + s), (kfill[s] - 1) & 1);
+        for (int s = 0; s < T::NSV; ++s)
+            if (vfill[s] > 0) mbar_wait_drain(bar(Bars::V_FULL + s), (vfill[s] - 1) & 1);
+    }
+}
+
+// ------------------------------------------------------------------- MMA
+template <class T>
+__device__ __forceinline__ void issue_qk(uint8_t* smem, uint32_t tmem, int t, int kslot) {
+    const uint32_t qa = smem_u32(smem + T::OFF_Q + t * T::Q_TILE);
+    const uint32_t kb = smem_u32(smem + T::OFF_K + kslot * T::K_TILE);
+    const uint32_t d = tmem + T::S_COL0 + t * T::BC;
+#pragma unroll
+    for (int kk = 0; kk < T::D / T::KSTEP; ++kk) {
+        const int box = kk / T::STEPS_PER_BOX, sub = kk % T::STEPS_PER_BOX;
+        const uint64_t ad = smem_desc(qa + box * T::Q_BOX_BYTES + sub * 32, 16, 8 * T::SW, T::LAYOUT);
+        const uint64_t bd = smem_desc(kb + box * T::K_BOX_BYTES + sub * 32, 16, 8 * T::SW, T::LAYOUT);
+        if constexpr (T::I8)
+            mma_i8_ss(d, ad, bd, T::IDESC_QK, kk > 0 ? 1u : 0u);
+        else
+            mma_f16_ss(d, ad, bd, T::IDESC_QK, kk > 0 ? 1u : 0u);
+    }
+}
+
+template <class T>
+__device__ __forceinline__ void issue_pv(uint8_t* smem, uint32_t tmem, int t, int vslot, bool accumulate,
+                                         uint32_t idesc_pv) {
+    const uint32_t vb = smem_u32(smem + T::OFF_V + vslot * T::V_TILE);
+    const uint32_t a_base = tmem + T::S_COL0 + t * T::BC;  // P aliases S
+    const uint32_t d = tmem + (T::I8 ? T::ACC_COL0 : T::O_COL0) + t * T::DVMAX;
+#pragma unroll
+    for (int kk = 0; kk < T::BC / T::KSTEP; ++kk) {
+        // MN-major V: 8-key atoms SBO = 8*SW apart, box (BOX columns) LBO = BC*SW apart
+        const uint64_t bd = smem_desc(vb + kk * T::KSTEP * T::SW, T::BC * T::SW, 8 * T::SW, T::LAYOUT);
+        const uint32_t acc = (kk > 0 || accumulate) ? 1u : 0u;
+        if constexpr (T::I8)
+            mma_i8_ts(d, a_base + kk * 8, bd, idesc_pv, acc);
+        else
+            mma_f16_ts(d, a_base + kk * 8, bd, idesc_pv, acc);
+    }
+}
+
+template <class T>
+__device__ void mma_role(const Params& p, const Work& w, int jlo, int jhi, const int* ta, const int* te,
+                         uint8_t* smem, uint32_t tmem, const Abort& ab, int dv) {
+    const uint32_t bars = smem_u32(smem);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+    const int kready = p.has_rope ? Bars::K_READY : Bars::K_FULL;
+    const uint32_t idesc_pv = instr_desc(T::I8 ? 2u : 1u, T::I8 ? 1u : 0u, 1u, BM, static_cast<uint32_t>(dv));
+    bool ok = mbar_wait(bar(p.has_rope ? Bars::Q_READY : Bars::Q_FULL), 0, ab, SITE_MMA_Q);
+    tc_fence_after();
+    int kc = 0, vc = 0;
+    int pc[2] = {0, 0};
+    if (ok && jlo < jhi) {
+        if (!mbar_wait(bar(kready + 0), 0, ab, SITE_MMA_K)) ok = false;
+        if (ok) {
+            tc_fence_after();
+            for (int t = 0; t < T::NT; ++t) {
+                if (ta[t] <= jlo && jlo < te[t]) {
+                    issue_qk<T>(smem, tmem, t, 0);
+                    tc_commit(bar(Bars::S_FULL + t));
+                }
+            }
+            tc_commit(bar(Bars::K_EMPTY + 0));
+            kc = 1;
+        }
+    }
+    for (int j = jlo; ok && j < jhi; ++j) {
+        const int vs = vc % T::NSV;
+        if (!mbar_wait(bar(Bars::V_FULL + vs), (vc / T::NSV) & 1, ab, SITE_MMA_V)) {
+            ok = false;
+            break;
+        }
+        const bool has_next = j + 1 < jhi;
+        const int ks = kc % T::NSK;
+        if (has_next && !mbar_wait(bar(kready + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+            ok = false;
+            break;
+        }
+        tc_fence_after();
+        for (int t = 0; t < T::NT; ++t) {
+            const bool act = ta[t] <= j && j < te[t];
+            const bool act_next = has_next && ta[t] <= j + 1 && j + 1 < te[t];
+            if (act) {
+                if (!mbar_wait(bar(Bars::P_FULL + t), pc[t] & 1, ab, SITE_MMA_P)) {
+                    ok = false;
+                    break;
+                }
+                pc[t]++;
+                tc_fence_after();
+                issue_pv<T>(smem, tmem, t, vs, j > ta[t], idesc_pv);
+                if (j == te[t] - 1) tc_commit(bar(Bars::O_FULL + t));
+            }
+            if (act_next) {
+                issue_qk<T>(smem, tmem, t, ks);
+                tc_commit(bar(Bars::S_FULL + t));
+            }
+        }
+        if (!ok) break;
+        tc_commit(bar(Bars::V_EMPTY + vs));
+        vc++;
+        if (has_next) {
+            tc_commit(bar(Bars::K_EMPTY + ks));
+            kc++;
+        }
+    }
+    // drain: no MMA may still be writing TMEM when the CTA releases it
+    tc_commit(bar(Bars::DRAIN));
+    mbar_wait_drain(bar(Bars::DRAIN), 0);
+}
+
+// ------------------------------------------------------------------ RoPE
+// Rotates rows [0, nrows) of a swizzled FP16 tile in place; row r sits at
+// sequence position pos0 + r.  Interleaved pairs (x[2i], x[2i+1]) rotate by
+// the angle in table column i (src/rdna/fa2_forward_f16.hip:63-77), result
+// rounded to fp16.
+template <class T>
+__device__ __forceinline__ void rope_tile(uint8_t* tile, int box_bytes, int nrows, int pos0, const float* cos_t,
+                                          const float* sin_t, int tid, int nthreads) {
+    constexpr int CPR = T::D / 8;            // 16-byte chunks per row
+    constexpr int CPB = T::SW / 16;          // chunks per box row
+    const int total = nrows * CPR;
+    for (int i = tid; i < total; i += nthreads) {
+        const int row = i / CPR, ch = i % CPR;
+        const int box = ch / CPB, cb = ch % CPB;
+        uint4* ptr = reinterpret_cast<uint4*>(tile + box * box_bytes + swz_off<T::SW>(row, cb));
+        const int pair0 = ch * 4;
+        const int64_t toff = static_cast<int64_t>(pos0 + row) * (T::D / 2) + pair0;
+        const float4 c = __ldg(reinterpret_cast<const float4*>(cos_t + toff));
+        const float4 s = __ldg(reinterpret_cast<const float4*>(sin_t + toff));
+        uint4 v = *ptr;
+        uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+        const float cc[4] = {c.x, c.y, c.z, c.w};
+        const float ss[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __half2 h = *reinterpret_cast<const __half2*>(&u[k]);
+            const float a = __low2float(h), b = __high2float(h);
+            const float x0 = a * cc[k] - b * ss[k];
+            const float x1 = a * ss[k] + b * cc[k];
+            u[k] = pack_half2(x0, x1);
+        }
+        *ptr = v;
+    }
+}
+
+template <class T>
+__device__ void rope_role(const Params& p, const Work& w, int jlo, int jhi, uint8_t* smem, const Abort& ab) {
+    if constexpr (!T::I8) {
+        const uint32_t bars = smem_u32(smem);
+        auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+        const int tid = threadIdx.x - 32 * T::WARP_ROPE0;
+        const int lane = threadIdx.x % 32;
+        if (!mbar_wait(bar(Bars::Q_FULL), 0, ab, SITE_ROPE_Q)) return;
+        for (int t = 0; t < T::NT; ++t) {
+            if (!w.valid[t]) continue;
+            const int nrows = min(BM, p.S - w.row0[t]);
+            rope_tile<T>(smem + T::OFF_Q + t * T::Q_TILE, T::Q_BOX_BYTES, nrows, w.row0[t], p.rot_cos, p.rot_sin, tid,
+                         64);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(Bars::Q_READY));
+        int i = 0;
+        for (int j = jlo; j < jhi; ++j, ++i) {
+            const int ks = i % T::NSK;
+            if (!mbar_wait(bar(Bars::K_FULL + ks), (i / T::NSK) & 1, ab, SITE_ROPE_K)) return;
+            const int nrows = min(T::BC, p.KS - j * T::BC);
+            rope_tile<T>(smem + T::OFF_K + ks * T::K_TILE, T::K_BOX_BYTES, nrows, j * T::BC, p.rot_cos, p.rot_sin,
+                         tid, 64);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(Bars::K_READY + ks));
+        }
+    }
+}
+
+// ---------------------------------------------------------------- kernel
+template <class T>
+__global__ void __launch_bounds__(T::THREADS, 1)
+    fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                      const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x / 32;
+    const uint32_t bars = smem_u32(smem);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Bars::ABORT_SLOT);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Bars::TMEM_SLOT);
+
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        mbar_init(bar(Bars::Q_FULL), 1);
+        mbar_init(bar(Bars::Q_READY), 2);
+        mbar_init(bar(Bars::DRAIN), 1);
+        for (int s = 0; s < T::NSK; ++s) {
+            mbar_init(bar(Bars::K_FULL + s), 1);
+            mbar_init(bar(Bars::K_READY + s), 2);
+            mbar_init(bar(Bars::K_EMPTY + s), 1);
+        }
+        for (int s = 0; s < T::NSV; ++s) {
+            mbar_init(bar(Bars::V_FULL + s), 1);
+            mbar_init(bar(Bars::V_EMPTY + s), 1);
+        }
+        for (int t = 0; t < T::NT; ++t) {
+            mbar_init(bar(Bars::S_FULL + t), 1);
+            mbar_init(bar(Bars::P_FULL + t), 4);
+            mbar_init(bar(Bars::O_FULL + t), 1);
+            mbar_init(bar(Bars::KS_FULL + 2 * t), 128);
+            mbar_init(bar(Bars::KS_FULL + 2 * t + 1), 128);
+            mbar_init(bar(Bars::EPI + t), 128);
+        }
+        fence_barrier_init();
+    }
+    if (warp == T::WARP_MMA) {
+        tmem_alloc(smem_u32(tmem_slot), T::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const Abort ab{abort_flag};
+
+    const Work w = decode_work<T>(p, blockIdx.x);
+    int dv = T::DVMAX, dv0 = 0;
+    if (p.n_split > 1) {
+        dv0 = w.split * p.dv_split;
+        dv = min(p.dv_split, T::D - dv0);
+    } else {
+        dv = T::D < T::DVMAX ? T::D : T::DVMAX;
+    }
+    int ta[2] = {0, 0}, te[2] = {0, 0};
+    for (int t = 0; t < T::NT; ++t) tile_blocks<T>(p, w.row0[t], w.valid[t], ta[t], te[t]);
+    int jlo = 1 << 30, jhi = -1;
+    for (int t = 0; t < T::NT; ++t) {
+        if (te[t] > ta[t]) {
+            jlo = min(jlo, ta[t]);
+            jhi = max(jhi, te[t]);
+        }
+    }
+    if (jhi < 0) jlo = jhi = 0;
+
+    if (warp < 4 * T::NT) {
+        softmax_role<T>(p, &tmO, w, warp / 4, smem, tmem, ab, dv, dv0);
+        tc_fence_before();
+    } else if (warp == T::WARP_PROD) {
+        if (sm100::lane_id() == 0) producer_role<T>(p, &tmQ, &tmK, &tmV, w, jlo, jhi, smem, ab, dv, dv0);
+    } else if (warp == T::WARP_MMA) {
+        if (sm100::lane_id() == 0) mma_role<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv);
+        __syncwarp();
+    } else if (p.has_rope) {
+        rope_role<T>(p, w, jlo, jhi, smem, ab);
+    }
+    __syncthreads();
+    if (warp == T::WARP_MMA) {
+        tc_fence_after();
+        tmem_dealloc(tmem, T::TMEM_COLS);
+    }
+}
+
+}  // namespace prefill
+}  // namespace rdna
