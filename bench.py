@@ -1,0 +1,475 @@
+"""Benchmark of the FA2 forward hot path on B200, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
+
+Workload (default): BASELINE config 2, the Llama-3-8B-shaped causal GQA
+prefill in FP16 (B=4, Hq=32, Hkv=8, S=4096, D=128, RoPE theta=5e5 applied
+in-kernel).  A step is one rdna_attention_forward call over the whole batch.
+Scaling is weak: every rank owns its own shard of (batch, KV-head group)
+units of the size of the single-GPU workload (global batch = 4 * N); no
+collective runs in the timed region.  `value` is total FLOPs of all ranks
+over the max-over-ranks device time; FLOPs count exactly the visible
+(query, key) pairs, both GEMMs at 2 FLOP/MAC (tests/benchmark.py:77-88).
+
+Inputs are synthetic N(0,1) fp16 (seed 0); 335 MB per step stays resident
+in HBM (larger than the 126 MB L2), so no L2 flush is needed between steps.
+`e2e` times the same call through the public Python API with the step's
+inputs copied in from pinned host memory and the output read back.
+`--impl reference` times the CPU restatement of the reference's algorithm
+(oracle/torch_oracle.py: fp32 torch on the host cores; the reference itself
+is HIP-only and cannot run here) on one query head of the same workload
+per step.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    "1": dict(workload="cfg1_mha_b1_h8_s512_d64", B=1, H=8, Hkv=8, S=512, KS=512, D=64, causal=False, window=-1,
+              theta=None, kind="fp16"),
+    "2": dict(workload="cfg2_llama3_8b_gqa_causal_prefill_s4096_rope", B=4, H=32, Hkv=8, S=4096, KS=4096, D=128,
+              causal=True, window=-1, theta=500000.0, kind="fp16"),
+    "3": dict(workload="cfg3_int8_b8_h16_s2048_d64_pertoken_qk_perchannel_v", B=8, H=16, Hkv=16, S=2048, KS=2048,
+              D=64, causal=False, window=-1, theta=None, kind="int8"),
+    "4a": dict(workload="cfg4a_sliding_causal_w4096_s16384_rope", B=1, H=32, Hkv=8, S=16384, KS=16384, D=128,
+               causal=True, window=4096, theta=1e6, kind="fp16"),
+    "4b": dict(workload="cfg4b_two_sided_pm1024_s8192_rope", B=1, H=32, Hkv=8, S=8192, KS=8192, D=128,
+               causal=False, window=2048, theta=1e6, kind="fp16"),
+    "5": dict(workload="cfg5_decode_s1_ks32768_b64_h64_kv8_bshd_cache", B=64, H=64, Hkv=8, S=1, KS=32768, D=128,
+              causal=False, window=-1, theta=None, kind="decode"),
+}
+
+NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+                0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+                0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+def metric_of(cfg):
+    if cfg["kind"] == "decode":
+        return "decode HBM GB/s", "GB/s"
+    if cfg["kind"] == "int8":
+        return "attention fwd TOPS (INT8)", "TOP/s"
+    return "attention fwd TFLOPS (FP16)", "TFLOP/s"
+
+
+def work_units(cfg, B=None):
+    """Algorithmic work of one step: FLOPs (prefill) or HBM bytes (decode)."""
+    from oracle.torch_oracle import flops  # pure arithmetic helper (pair counting)
+
+    B = cfg["B"] if B is None else B
+    if cfg["kind"] == "decode":
+        kv = 2 * B * cfg["Hkv"] * cfg["KS"] * cfg["D"] * 2
+        qo = 2 * B * cfg["H"] * cfg["S"] * cfg["D"] * 2
+        return kv + qo
+    return flops(B, cfg["H"], cfg["S"], cfg["KS"], cfg["D"], cfg["causal"], cfg["window"])
+
+
+def algorithmic_bytes(cfg):
+    e = 1 if cfg["kind"] == "int8" else 2
+    q = cfg["B"] * cfg["H"] * cfg["S"] * cfg["D"] * e
+    kv = 2 * cfg["B"] * cfg["Hkv"] * cfg["KS"] * cfg["D"] * e
+    o = cfg["B"] * cfg["H"] * cfg["S"] * cfg["D"] * 2
+    return q + kv + o
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Polls NVML SM clock and clock-event reasons on a thread while running."""
+
+    def __init__(self, index):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception:
+            self._ok = False
+
+    def _reasons(self):
+        nv = self._nv
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        return fn(self._h)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                self.reasons |= int(self._reasons())
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self._ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self._ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"]}
+        names = [n for bit, n in NVML_REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- inputs
+def make_inputs(cfg, device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, H, Hkv, S, KS, D = cfg["B"], cfg["H"], cfg["Hkv"], cfg["S"], cfg["KS"], cfg["D"]
+    q = torch.randn(B, H, S, D, generator=g, device=device, dtype=torch.float16)
+    if cfg["kind"] == "decode":
+        # KV cache stored [B, KS, Hkv, D], viewed [B, Hkv, KS, D] through strides
+        kc = torch.randn(B, KS, Hkv, D, generator=g, device=device, dtype=torch.float16)
+        vc = torch.randn(B, KS, Hkv, D, generator=g, device=device, dtype=torch.float16)
+        return dict(q=q, k=kc.transpose(1, 2), v=vc.transpose(1, 2), kc=kc, vc=vc)
+    k = torch.randn(B, Hkv, KS, D, generator=g, device=device, dtype=torch.float16)
+    v = torch.randn(B, Hkv, KS, D, generator=g, device=device, dtype=torch.float16)
+    out = dict(q=q, k=k, v=v)
+    if cfg["theta"]:
+        rows = max(S, KS)
+        pos = torch.arange(rows, device=device).unsqueeze(1).float()
+        inv = cfg["theta"] ** (-torch.arange(0, D, 2, device=device).float() / D)
+        ang = pos * inv
+        out["cos"], out["sin"] = ang.cos().contiguous(), ang.sin().contiguous()
+    if cfg["kind"] == "int8":
+        import rdnattention_b200 as R
+
+        _, _, vi, _, _, vs, vch = R.quantize_int8_perchannel_v(q, k, v)
+        qi, ki, qsc, ksc = R.quantize_int8_qk_pertoken(q, k)
+        out.update(qi=qi, ki=ki, vi=vi, qsc=qsc, ksc=ksc, vs=vs)
+    return out
+
+
+def step_fn(cfg, x):
+    """One hot-path pass over resident device inputs (the launch the device timing measures)."""
+    import rdnattention_b200 as R
+
+    if cfg["kind"] == "int8":
+        return lambda: R.flash_attn_int8qk(x["qi"], x["ki"], x["vi"], x["qsc"], x["ksc"], x["vs"])
+    if cfg["kind"] == "decode":
+        out = torch.empty_like(x["q"])
+        return lambda: R.flash_attn_strided(x["q"], x["k"], x["v"], out=out)
+    out = torch.empty_like(x["q"])
+    return lambda: R.flash_attn_strided(x["q"], x["k"], x["v"], is_causal=cfg["causal"],
+                                        window_size=cfg["window"], rot_cos=x.get("cos"), rot_sin=x.get("sin"),
+                                        out=out)
+
+
+# ---------------------------------------------------------------- timing
+def barrier(dist_on):
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def time_device(fn, steps, warmup, dist_on, sampler=None):
+    for _ in range(warmup):
+        fn()
+    barrier(dist_on)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+    barrier(dist_on)
+    ms = start.elapsed_time(end)
+    if dist_on:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    return ms
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        pass
+
+
+def time_e2e(cfg, x, steps, warmup, dist_on):
+    """Public API with host buffers: per step H2D of the inputs from pinned memory,
+    the attention call, D2H of the output; timed with events on the current stream."""
+    import rdnattention_b200 as R
+
+    host = {}
+    names = ["qi", "ki", "vi", "qsc", "ksc"] if cfg["kind"] == "int8" else ["q", "k", "v"]
+    if cfg["kind"] == "decode":
+        names = ["q", "kc", "vc"]
+    if cfg["kind"] == "fp16" and "cos" in x:
+        names += ["cos", "sin"]
+    for n in names:
+        host[n] = x[n].detach().to("cpu").pin_memory()
+    dev = {n: torch.empty_like(x[n]) for n in names}
+    out_host = torch.empty(x["q"].shape, dtype=torch.float16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def once():
+        for n in names:
+            dev[n].copy_(host[n], non_blocking=True)
+        if cfg["kind"] == "int8":
+            o = R.flash_attn_int8qk(dev["qi"], dev["ki"], dev["vi"], dev["qsc"], dev["ksc"], x["vs"])
+        elif cfg["kind"] == "decode":
+            o = R.flash_attn_strided(dev["q"], dev["kc"].transpose(1, 2), dev["vc"].transpose(1, 2))
+        else:
+            o = R.flash_attn(dev["q"], dev["k"], dev["v"], is_causal=cfg["causal"], window_size=cfg["window"],
+                             rot_cos=dev.get("cos"), rot_sin=dev.get("sin"))
+        out_host.copy_(o, non_blocking=True)
+
+    ms = time_device(once, steps, warmup, dist_on)
+    return ms, h2d, d2h
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_baseline(cfg, max_seconds=10.0):
+    """The oracle port (fp32 torch on the host cores) on a bounded sample: whole query
+    heads of batch 0 of the same workload, until ~max_seconds of CPU work."""
+    from oracle import torch_oracle
+
+    g = torch.Generator().manual_seed(0)
+    B, H, Hkv, S, KS, D = 1, cfg["H"], cfg["Hkv"], cfg["S"], cfg["KS"], cfg["D"]
+    G = H // Hkv
+    q = torch.randn(1, G, S, D, generator=g).half()  # heads of kv group 0
+    k = torch.randn(1, 1, KS, D, generator=g).half()
+    v = torch.randn(1, 1, KS, D, generator=g).half()
+    cos = sin = None
+    if cfg["theta"]:
+        pos = torch.arange(max(S, KS)).unsqueeze(1).float()
+        inv = cfg["theta"] ** (-torch.arange(0, D, 2).float() / D)
+        cos, sin = (pos * inv).cos(), (pos * inv).sin()
+    from oracle.torch_oracle import flops as _fl
+
+    done_units, heads = 0.0, 0
+    t0 = time.perf_counter()
+    while heads < G and (time.perf_counter() - t0) < max_seconds:
+        torch_oracle.attention(q, k, v, causal=cfg["causal"], window=cfg["window"], rot_cos=cos, rot_sin=sin,
+                               heads=range(heads, heads + 1))
+        heads += 1
+    secs = time.perf_counter() - t0
+    if cfg["kind"] == "decode":
+        done_units = 2 * KS * D * 2 + 2 * S * D * 2 * heads  # bytes of the sampled heads' K/V + q/o
+        value = done_units / secs / 1e9
+    else:
+        done_units = _fl(1, heads, S, KS, D, cfg["causal"], cfg["window"])
+        value = done_units / secs / 1e12
+    return {"value": value, "unit": metric_of(cfg)[1], "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{heads} query head(s) of batch 0 / kv group 0, fp32 torch oracle, {secs:.2f} s",
+            "host_cpu_count": os.cpu_count()}
+
+
+# ---------------------------------------------------------------- roofline
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def load_traffic(workload):
+    """DRAM bytes per launch from a committed ncu summary (profiles/<kernel>_<workload>.txt)."""
+    for f in (ROOT / "profiles").glob("*.txt"):
+        txt = f.read_text()
+        if f"workload: {workload}" not in txt:
+            continue
+        for line in txt.splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                try:
+                    return float(line.split(":", 1)[1].strip())
+                except ValueError:
+                    return None
+    return None
+
+
+# ---------------------------------------------------------------- main
+def run_reference(args, cfg):
+    """CPU arm: the oracle port of the reference algorithm, one query head of the
+    workload per step, on all host threads."""
+    from oracle import torch_oracle
+    from oracle.torch_oracle import flops
+
+    metric, unit = metric_of(cfg)
+    g = torch.Generator().manual_seed(0)
+    S, KS, D, G = cfg["S"], cfg["KS"], cfg["D"], cfg["H"] // cfg["Hkv"]
+    q = torch.randn(1, G, S, D, generator=g).half()
+    k = torch.randn(1, 1, KS, D, generator=g).half()
+    v = torch.randn(1, 1, KS, D, generator=g).half()
+    cos = sin = None
+    if cfg["theta"]:
+        pos = torch.arange(max(S, KS)).unsqueeze(1).float()
+        inv = cfg["theta"] ** (-torch.arange(0, D, 2).float() / D)
+        cos, sin = (pos * inv).cos(), (pos * inv).sin()
+
+    def one(i):
+        h = i % G
+        torch_oracle.attention(q, k, v, causal=cfg["causal"], window=cfg["window"], rot_cos=cos, rot_sin=sin,
+                               heads=range(h, h + 1))
+
+    for i in range(args.warmup):
+        one(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one(i)
+    secs = time.perf_counter() - t0
+    if cfg["kind"] == "decode":
+        per = 2 * KS * D * 2 + 2 * S * D * 2
+        value = per * args.steps / secs / 1e9
+    else:
+        per = flops(1, 1, S, KS, D, cfg["causal"], cfg["window"])
+        value = per * args.steps / secs / 1e12
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3 / max(args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": cfg["workload"], "sample_per_step": "one query head (fp32 torch oracle)"},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": "one query head of batch 0 per step, fp32 torch restatement of "
+                                       "tests/accuracy.py dense_attention_reference + masks + RoPE"},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None, help="override the per-rank batch (profiling runs)")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    if args.batch is not None:
+        cfg["B"] = args.batch
+        cfg["workload"] += f"_b{args.batch}"
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, cfg)
+        return
+
+    dist_on = world > 1
+    torch.cuda.set_device(local)
+    if dist_on:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    import rdnattention_b200 as R
+
+    R.library_path()  # fail loudly if the CUDA library is missing
+    x = make_inputs(cfg, "cuda", seed=1000 + rank)
+    fn = step_fn(cfg, x)
+
+    sampler = ClockSampler(local)
+    ms = time_device(fn, args.steps, args.warmup, dist_on, sampler)
+    status = R.debug_read_status()
+    per_step_units = work_units(cfg)
+    total_units = per_step_units * world * args.steps
+    scale = 1e9 if cfg["kind"] == "decode" else 1e12
+    value = total_units / (ms / 1e3) / scale
+    ms_step = ms / args.steps
+
+    e2e = None
+    if not args.no_e2e:
+        e2e_steps = args.e2e_steps or max(3, min(args.steps, 20))
+        e2e_ms, h2d, d2h = time_e2e(cfg, x, e2e_steps, min(args.warmup, 3), dist_on)
+        e2e_value = per_step_units * world * e2e_steps / (e2e_ms / 1e3) / scale
+        e2e = {"value": e2e_value, "unit": metric_of(cfg)[1], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "steps": e2e_steps}
+
+    # all-gather of O across ranks (result assembly; outside the timed region)
+    collective = None
+    if dist_on:
+        o = torch.empty_like(x["q"])
+        gathered = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=o.device)
+        for _ in range(2):
+            torch.distributed.all_gather_into_tensor(gathered, o)
+        c_ms = time_device(lambda: torch.distributed.all_gather_into_tensor(gathered, o), 5, 0, dist_on)
+        collective = {"op": "nccl all_gather of O", "ms": c_ms / 5, "bytes_per_rank": o.numel() * 2}
+
+    if rank != 0:
+        if dist_on:
+            torch.distributed.destroy_process_group()
+        return
+
+    metric, unit = metric_of(cfg)
+    peak_tc, peak_hbm, peak_src = load_peaks()
+    if cfg["kind"] == "decode":
+        roof = {"bound": "hbm", "achieved": per_step_units / (ms_step / 1e3) / 1e9, "peak": peak_hbm,
+                "unit": "GB/s"}
+    else:
+        peak = peak_tc * (2 if cfg["kind"] == "int8" else 1)
+        roof = {"bound": "tensor", "achieved": per_step_units / (ms_step / 1e3) / 1e12, "peak": peak,
+                "unit": "TOP/s" if cfg["kind"] == "int8" else "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_source"] = f"{peak_src} (MEASURED_PEAKS.json bf16 burst{' x2 for int8' if cfg['kind']=='int8' else ''})"
+    roof["traffic"] = load_traffic(cfg["workload"])
+    roof["algorithmic_bytes"] = algorithmic_bytes(cfg)
+
+    line = {
+        "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8" if cfg["kind"] == "int8" else "fp16", "data": "synthetic",
+        "config": {"workload": cfg["workload"], "B_per_rank": cfg["B"], "H": cfg["H"], "Hkv": cfg["Hkv"],
+                   "S": cfg["S"], "KS": cfg["KS"], "D": cfg["D"], "causal": cfg["causal"], "window": cfg["window"],
+                   "rope_theta": cfg["theta"], "global_batch": cfg["B"] * world,
+                   "parallelism": f"shard (batch, kv-head group) units x{world}",
+                   "l2": "inputs larger than L2, no flush"},
+        "clocks": sampler.summary(),
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "roofline": roof,
+        "kernel_status": list(status),
+    }
+    if collective:
+        line["collective"] = collective
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+    if dist_on:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

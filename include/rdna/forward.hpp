@@ -4,6 +4,7 @@
 // against librdnattention.so unchanged.
 #pragma once
 
+#include <cstddef>
 #include <cstdint>
 
 namespace rdna {
@@ -60,7 +61,13 @@ struct ForwardParamsInt8QK {
 };
 
 /// Enqueues the FP16 forward on `stream` (a cudaStream_t). Non-blocking. 0 on success.
+/// With RoPE it takes a stream-ordered workspace (cudaMallocAsync / cudaFreeAsync).
 int forwardF16(const ForwardParams& params, void* stream);
+/// Device workspace forwardF16Ws() needs for these parameters (0 without RoPE).
+size_t workspaceBytesF16(const ForwardParams& params);
+/// forwardF16 with a caller-provided workspace (256-byte aligned, at least
+/// workspaceBytesF16() bytes; may be null when that is 0).  Allocates nothing.
+int forwardF16Ws(const ForwardParams& params, void* workspace, size_t workspace_bytes, void* stream);
 /// Reason the most recent forwardF16() call on this thread failed, or nullptr.
 const char* lastError();
 /// Enqueues the INT8 forward on `stream`. Non-blocking. 0 on success.

@@ -8,9 +8,11 @@
  * unchanged.  Device pointers are CUDA device pointers and `stream` is a
  * cudaStream_t (the reference's hipStream_t slot).
  *
- * Every function operates on caller-owned device memory; the library keeps
- * no handle table and allocates no device memory.  Launches are enqueued on
- * `stream` and never block the host.
+ * Every function operates on caller-owned device memory and keeps no handle
+ * table.  Launches are enqueued on `stream` and never block the host.  The
+ * only device memory the library obtains itself is the RoPE workspace of
+ * rdna_attention_forward (stream-ordered; see rdna_attention_forward_ws for
+ * the variant that takes it from the caller).
  */
 #ifndef RDNATTENTION_H_
 #define RDNATTENTION_H_
@@ -80,6 +82,31 @@ RDNA_API int32_t rdna_attention_forward_int8qk(
     int32_t causal, int32_t window_size, void* stream);
 
 /* ---- Extensions beyond the reference ABI (no counterpart there) ---- */
+
+/* Bytes of device workspace rdna_attention_forward_ws() needs for this
+ * problem: 0 without RoPE; with RoPE, room for the rotated Q and K (fp16),
+ * which a pre-pass writes once per call so the attention tiles arrive
+ * rotated.  (rdna_attention_forward itself obtains that workspace with
+ * cudaMallocAsync/cudaFreeAsync on `stream`.) */
+RDNA_API uint64_t rdna_attention_forward_workspace_size(
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim, int32_t has_rope);
+
+/* rdna_attention_forward with a caller-owned workspace (256-byte aligned,
+ * at least rdna_attention_forward_workspace_size() bytes; may be NULL when
+ * that size is 0): the library then allocates nothing.  Same arguments and
+ * return codes otherwise. */
+RDNA_API int32_t rdna_attention_forward_ws(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* Reads and clears the device status word of the current device: out[0] =
  * first error code a kernel recorded (a bounded wait that expired), out[1] =

@@ -61,6 +61,11 @@ def _lib_handle():
         lib.rdna_get_error.restype = ctypes.c_char_p
         lib.rdna_attention_forward.argtypes = [vp] * 6 + [i64] * 12 + [u32] * 6 + [f32, i32, i32, i32, vp]
         lib.rdna_attention_forward.restype = i32
+        lib.rdna_attention_forward_ws.argtypes = ([vp] * 6 + [i64] * 12 + [u32] * 6 + [f32, i32, i32, i32]
+                                                  + [vp, ctypes.c_uint64, vp])
+        lib.rdna_attention_forward_ws.restype = i32
+        lib.rdna_attention_forward_workspace_size.argtypes = [u32] * 6 + [i32]
+        lib.rdna_attention_forward_workspace_size.restype = ctypes.c_uint64
         lib.rdna_attention_forward_int8qk.argtypes = ([vp] * 4 + [i64] * 12 + [u32] * 6 + [f32] * 4 + [vp, vp]
                                                       + [i32, i32, vp])
         lib.rdna_attention_forward_int8qk.restype = i32
@@ -160,11 +165,17 @@ def _fp16_forward(query, key, value, is_causal, window_size, rot_cos, rot_sin, o
     if scale is None:
         scale = head_dim ** -0.5
     qs, ks, vs, os_ = query.stride(), key.stride(), value.stride(), out.stride()
-    rc = _lib_handle().rdna_attention_forward(
+    lib = _lib_handle()
+    # RoPE runs as a pre-pass into a workspace; take it from torch's caching allocator
+    ws_bytes = lib.rdna_attention_forward_workspace_size(batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+                                                         has_rope)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=query.device) if ws_bytes else None
+    rc = lib.rdna_attention_forward_ws(
         query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(), cos_p, sin_p,
         qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
         batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
-        float(scale), 1 if is_causal else 0, has_rope, int(window_size), _stream_handle(query.device))
+        float(scale), 1 if is_causal else 0, has_rope, int(window_size),
+        ws.data_ptr() if ws is not None else None, ws_bytes, _stream_handle(query.device))
     if rc != 0:
         raise RDNAttentionError(f"flash_attn failed: {_last_error()}")
     return out

@@ -29,7 +29,9 @@ RDNA_API int32_t rdna_has_device(void) { return rdna::hasDevice() ? 1 : 0; }
 
 RDNA_API const char* rdna_get_error(void) { return g_error.data(); }
 
-RDNA_API int32_t rdna_attention_forward(
+namespace {
+
+rdna::ForwardParams f16_params(
     const void* q, const void* k, const void* v, void* output,
     const void* rot_cos, const void* rot_sin,
     int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
@@ -38,8 +40,7 @@ RDNA_API int32_t rdna_attention_forward(
     int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
     uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
     uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
-    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
-    void* stream) {
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size) {
     rdna::ForwardParams p{};
     p.q = q;
     p.k = k;
@@ -69,7 +70,63 @@ RDNA_API int32_t rdna_attention_forward(
     p.causal = causal != 0 ? 1u : 0u;
     p.hasRope = has_rope != 0 ? 1u : 0u;
     p.windowSize = window_size;
+    return p;
+}
+
+}  // namespace
+
+RDNA_API int32_t rdna_attention_forward(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* stream) {
+    const rdna::ForwardParams p = f16_params(q, k, v, output, rot_cos, rot_sin, q_stride_b, q_stride_h, q_stride_s,
+                                             k_stride_b, k_stride_h, k_stride_s, v_stride_b, v_stride_h, v_stride_s,
+                                             o_stride_b, o_stride_h, o_stride_s, batch_size, num_heads, num_kv_heads,
+                                             seq_len, key_seq_len, head_dim, scale, causal, has_rope, window_size);
     if (rdna::forwardF16(p, stream) != 0) {
+        set_error("Attention (fp16) failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API uint64_t rdna_attention_forward_workspace_size(
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim, int32_t has_rope) {
+    rdna::ForwardParams p{};
+    p.batchSize = batch_size;
+    p.numHeads = num_heads;
+    p.numKvHeads = num_kv_heads;
+    p.seqLen = seq_len;
+    p.keySeqLen = key_seq_len;
+    p.headDim = head_dim;
+    p.hasRope = has_rope != 0 ? 1u : 0u;
+    return rdna::workspaceBytesF16(p);
+}
+
+RDNA_API int32_t rdna_attention_forward_ws(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* workspace, uint64_t workspace_bytes, void* stream) {
+    const rdna::ForwardParams p = f16_params(q, k, v, output, rot_cos, rot_sin, q_stride_b, q_stride_h, q_stride_s,
+                                             k_stride_b, k_stride_h, k_stride_s, v_stride_b, v_stride_h, v_stride_s,
+                                             o_stride_b, o_stride_h, o_stride_s, batch_size, num_heads, num_kv_heads,
+                                             seq_len, key_seq_len, head_dim, scale, causal, has_rope, window_size);
+    if (rdna::forwardF16Ws(p, workspace, workspace_bytes, stream) != 0) {
         set_error("Attention (fp16) failed: %s", rdna::lastError());
         return -3;
     }

@@ -19,8 +19,14 @@
 //                     O_t += P_t V (TS form, P read from TMEM).  Per block j
 //                     it issues, for each tile, PV(j) then QK(j+1), so one
 //                     tile's softmax overlaps the other tile's MMAs.
-//   warps 4*NT+2..+3  RoPE: rotate Q tiles once and every K tile in shared
-//                     memory (interleaved pairs) before the MMA reads them.
+//   warps 4*NT+2..+3  idle; they complete the control warpgroup so that the
+//                     NT = 2 kernel can move registers from it to the softmax
+//                     warpgroups (setmaxnreg: 200 / 80 per thread, launched
+//                     at 168).
+//
+// RoPE is not applied here: rope.cuh rotates Q and K once per launch and the
+// kernel reads the rotated copies (rotating inside every CTA would repeat the
+// K rotation once per query tile that reads the block).
 //
 // TMEM columns: S_t at [t*BC, t*BC+BC) (P aliases its first columns);
 // FP16: O_t (fp32) after all S.  INT8: ACC_t (s32 PV accumulator) then
@@ -51,15 +57,12 @@ struct Params {
     int delta;    // KS - S
     int causal;
     int window;   // <= 0: no window
-    int has_rope;
     int pair_heads;
     int n_rb;     // ceil(S / BM)
     int n_rp;     // ceil(n_rb / 2)
     int n_split;  // output column slices per tile (head_dim > 256)
     int dv_split; // output columns per slice (multiple of the box width)
     float scale_log2;
-    const float* rot_cos;
-    const float* rot_sin;
     // INT8 path
     float q_scale, k_scale, pv_scale;
     const float* q_vec;
@@ -92,7 +95,13 @@ struct Traits {
     static constexpr int THREADS = 128 * NT + 128;
     static constexpr int WARP_PROD = 4 * NT;
     static constexpr int WARP_MMA = 4 * NT + 1;
-    static constexpr int WARP_ROPE0 = 4 * NT + 2;
+    // Register split (NT = 2 only): launched at LAUNCH_REGS per thread.
+    static constexpr bool RESPLIT = NT == 2;
+    static constexpr int LAUNCH_REGS = 168;
+    static constexpr int SOFTMAX_REGS = 200;
+    static constexpr int CONTROL_REGS = 80;
+    static_assert(!RESPLIT || 256 * SOFTMAX_REGS + 128 * CONTROL_REGS <= THREADS * LAUNCH_REGS,
+                  "register split exceeds the launch allocation");
 
     // TMEM columns
     static constexpr int S_COL0 = 0;
@@ -132,9 +141,8 @@ struct Traits {
 
 // Barrier slots inside the misc region.
 struct Bars {
-    static constexpr int Q_FULL = 0, Q_READY = 1, DRAIN = 2;
+    static constexpr int Q_FULL = 0, DRAIN = 2;
     static constexpr int K_FULL = 4;      // +NSK
-    static constexpr int K_READY = 12;    // +NSK
     static constexpr int K_EMPTY = 20;    // +NSK
     static constexpr int V_FULL = 28;     // +NSV
     static constexpr int V_EMPTY = 36;    // +NSV
@@ -153,7 +161,6 @@ enum Site : int {
     SITE_PROD_KEMPTY = 0x101, SITE_PROD_VEMPTY = 0x102,
     SITE_MMA_Q = 0x201, SITE_MMA_K = 0x202, SITE_MMA_V = 0x203, SITE_MMA_P = 0x204,
     SITE_SM_S = 0x301, SITE_SM_O = 0x302, SITE_SM_Q = 0x303, SITE_SM_KS = 0x304, SITE_SM_EPI = 0x305,
-    SITE_ROPE_Q = 0x401, SITE_ROPE_K = 0x402,
 };
 
 struct Work {
@@ -494,9 +501,8 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
     const bool has_blocks = e > a;
     if (!aborted && has_blocks && !warp_wait(bar(Bars::O_FULL + t), 0, ab, SITE_SM_O)) aborted = true;
     if (!aborted) tc_fence_after();
-    // FP16 stages O in Q_t's buffer: its TMA load (and RoPE) must have landed
-    if (!aborted && !T::I8 && !warp_wait(bar(p.has_rope ? Bars::Q_READY : Bars::Q_FULL), 0, ab, SITE_SM_Q))
-        aborted = true;
+    // FP16 stages O in Q_t's buffer: its TMA load must have landed
+    if (!aborted && !T::I8 && !warp_wait(bar(Bars::Q_FULL), 0, ab, SITE_SM_Q)) aborted = true;
 
     uint8_t* stage = smem + T::OFF_O + t * T::O_STRIDE;
     if (!aborted) {
@@ -650,9 +656,9 @@ __device__ void mma_role(const Params& p, const Work& w, int jlo, int jhi, const
                          uint8_t* smem, uint32_t tmem, const Abort& ab, int dv) {
     const uint32_t bars = smem_u32(smem);
     auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
-    const int kready = p.has_rope ? Bars::K_READY : Bars::K_FULL;
+    const int kready = Bars::K_FULL;
     const uint32_t idesc_pv = instr_desc(T::I8 ? 2u : 1u, T::I8 ? 1u : 0u, 1u, BM, static_cast<uint32_t>(dv));
-    bool ok = mbar_wait(bar(p.has_rope ? Bars::Q_READY : Bars::Q_FULL), 0, ab, SITE_MMA_Q);
+    bool ok = mbar_wait(bar(Bars::Q_FULL), 0, ab, SITE_MMA_Q);
     tc_fence_after();
     int kc = 0, vc = 0;
     int pc[2] = {0, 0};
@@ -714,72 +720,6 @@ __device__ void mma_role(const Params& p, const Work& w, int jlo, int jhi, const
     mbar_wait_drain(bar(Bars::DRAIN), 0);
 }
 
-// ------------------------------------------------------------------ RoPE
-// Rotates rows [0, nrows) of a swizzled FP16 tile in place; row r sits at
-// sequence position pos0 + r.  Interleaved pairs (x[2i], x[2i+1]) rotate by
-// the angle in table column i (src/rdna/fa2_forward_f16.hip:63-77), result
-// rounded to fp16.
-template <class T>
-__device__ __forceinline__ void rope_tile(uint8_t* tile, int box_bytes, int nrows, int pos0, const float* cos_t,
-                                          const float* sin_t, int tid, int nthreads) {
-    constexpr int CPR = T::D / 8;            // 16-byte chunks per row
-    constexpr int CPB = T::SW / 16;          // chunks per box row
-    const int total = nrows * CPR;
-    for (int i = tid; i < total; i += nthreads) {
-        const int row = i / CPR, ch = i % CPR;
-        const int box = ch / CPB, cb = ch % CPB;
-        uint4* ptr = reinterpret_cast<uint4*>(tile + box * box_bytes + swz_off<T::SW>(row, cb));
-        const int pair0 = ch * 4;
-        const int64_t toff = static_cast<int64_t>(pos0 + row) * (T::D / 2) + pair0;
-        const float4 c = __ldg(reinterpret_cast<const float4*>(cos_t + toff));
-        const float4 s = __ldg(reinterpret_cast<const float4*>(sin_t + toff));
-        uint4 v = *ptr;
-        uint32_t* u = reinterpret_cast<uint32_t*>(&v);
-        const float cc[4] = {c.x, c.y, c.z, c.w};
-        const float ss[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const __half2 h = *reinterpret_cast<const __half2*>(&u[k]);
-            const float a = __low2float(h), b = __high2float(h);
-            const float x0 = a * cc[k] - b * ss[k];
-            const float x1 = a * ss[k] + b * cc[k];
-            u[k] = pack_half2(x0, x1);
-        }
-        *ptr = v;
-    }
-}
-
-template <class T>
-__device__ void rope_role(const Params& p, const Work& w, int jlo, int jhi, uint8_t* smem, const Abort& ab) {
-    if constexpr (!T::I8) {
-        const uint32_t bars = smem_u32(smem);
-        auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
-        const int tid = threadIdx.x - 32 * T::WARP_ROPE0;
-        const int lane = threadIdx.x % 32;
-        if (!mbar_wait(bar(Bars::Q_FULL), 0, ab, SITE_ROPE_Q)) return;
-        for (int t = 0; t < T::NT; ++t) {
-            if (!w.valid[t]) continue;
-            const int nrows = min(BM, p.S - w.row0[t]);
-            rope_tile<T>(smem + T::OFF_Q + t * T::Q_TILE, T::Q_BOX_BYTES, nrows, w.row0[t], p.rot_cos, p.rot_sin, tid,
-                         64);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(Bars::Q_READY));
-        int i = 0;
-        for (int j = jlo; j < jhi; ++j, ++i) {
-            const int ks = i % T::NSK;
-            if (!mbar_wait(bar(Bars::K_FULL + ks), (i / T::NSK) & 1, ab, SITE_ROPE_K)) return;
-            const int nrows = min(T::BC, p.KS - j * T::BC);
-            rope_tile<T>(smem + T::OFF_K + ks * T::K_TILE, T::K_BOX_BYTES, nrows, j * T::BC, p.rot_cos, p.rot_sin,
-                         tid, 64);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(Bars::K_READY + ks));
-        }
-    }
-}
-
 // ---------------------------------------------------------------- kernel
 template <class T>
 __global__ void __launch_bounds__(T::THREADS, 1)
@@ -797,11 +737,9 @@ __global__ void __launch_bounds__(T::THREADS, 1)
     if (threadIdx.x == 0) {
         *abort_flag = 0;
         mbar_init(bar(Bars::Q_FULL), 1);
-        mbar_init(bar(Bars::Q_READY), 2);
         mbar_init(bar(Bars::DRAIN), 1);
         for (int s = 0; s < T::NSK; ++s) {
             mbar_init(bar(Bars::K_FULL + s), 1);
-            mbar_init(bar(Bars::K_READY + s), 2);
             mbar_init(bar(Bars::K_EMPTY + s), 1);
         }
         for (int s = 0; s < T::NSV; ++s) {
@@ -847,16 +785,21 @@ __global__ void __launch_bounds__(T::THREADS, 1)
     }
     if (jhi < 0) jlo = jhi = 0;
 
+    if constexpr (T::RESPLIT) {
+        if (warp < 4 * T::NT)
+            regs_increase<T::SOFTMAX_REGS>();
+        else
+            regs_decrease<T::CONTROL_REGS>();
+    }
     if (warp < 4 * T::NT) {
         softmax_role<T>(p, &tmO, w, warp / 4, smem, tmem, ab, dv, dv0);
         tc_fence_before();
     } else if (warp == T::WARP_PROD) {
         if (sm100::lane_id() == 0) producer_role<T>(p, &tmQ, &tmK, &tmV, w, jlo, jhi, smem, ab, dv, dv0);
+        __syncwarp();
     } else if (warp == T::WARP_MMA) {
         if (sm100::lane_id() == 0) mma_role<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv);
         __syncwarp();
-    } else if (p.has_rope) {
-        rope_role<T>(p, w, jlo, jhi, smem, ab);
     }
     __syncthreads();
     if (warp == T::WARP_MMA) {

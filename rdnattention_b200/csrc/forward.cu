@@ -19,6 +19,7 @@
 
 #include "fa_decode.cuh"
 #include "fa_prefill.cuh"
+#include "rope.cuh"
 
 namespace rdna {
 namespace {
@@ -89,19 +90,22 @@ struct Common {
 bool fits_i32(int64_t s) { return s >= INT32_MIN && s <= INT32_MAX; }
 
 const char* check_common(const Common& c) {
-    if (c.q == nullptr || c.k == nullptr || c.v == nullptr || c.o == nullptr) return "null tensor pointer";
+    // with key_seq_len == 0 K and V are never read (an empty tensor may have a null pointer)
+    if (c.q == nullptr || c.o == nullptr || (c.KS > 0 && (c.k == nullptr || c.v == nullptr)))
+        return "null tensor pointer";
     if (c.B == 0 || c.H == 0 || c.S == 0) return "empty problem (batch_size, num_heads and seq_len must be > 0)";
     if (c.Hkv == 0 || c.H % c.Hkv != 0) return "numHeads must be a positive multiple of numKvHeads";
     if (!fits_i32(c.qs[2]) || !fits_i32(c.ks[2]) || !fits_i32(c.vs[2]) || !fits_i32(c.os[2]))
         return "sequence-axis stride exceeds int32 range - not a realistic tensor size for this kernel";
     const int64_t align_in = 16 / c.esz;  // elements per 16 bytes
     auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-    if (!aligned(c.q) || !aligned(c.k) || !aligned(c.v) || !aligned(c.o))
+    if (!aligned(c.q) || !aligned(c.o) || (c.KS > 0 && (!aligned(c.k) || !aligned(c.v))))
         return "tensor base pointers must be 16-byte aligned";
     const int64_t* in[3] = {c.qs, c.ks, c.vs};
     const uint64_t ext_q[3] = {c.B, c.H, c.S};
     const uint64_t ext_kv[3] = {c.B, c.Hkv, c.KS};
     for (int t = 0; t < 3; ++t) {
+        if (t > 0 && c.KS == 0) continue;  // K/V are never read
         const uint64_t* ext = t == 0 ? ext_q : ext_kv;
         for (int a = 0; a < 3; ++a) {
             if (ext[a] <= 1) continue;
@@ -124,10 +128,13 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
     CUtensorMap tmQ, tmK, tmV, tmO;
     const CUtensorMapSwizzle sw = T::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     const CUtensorMapSwizzle osw = T::O_SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-    const uint64_t ks_ext = c.KS > 0 ? c.KS : 1;
     const View4 vq{c.q, {c.D, c.S, c.H, c.B}, {c.qs[2], c.qs[1], c.qs[0]}};
-    const View4 vk{c.k, {c.D, ks_ext, c.Hkv, c.B}, {c.ks[2], c.ks[1], c.ks[0]}};
-    const View4 vv{c.v, {c.D, ks_ext, c.Hkv, c.B}, {c.vs[2], c.vs[1], c.vs[0]}};
+    // key_seq_len == 0: K/V are never read; give them a valid 1-row map
+    const bool nokv = c.KS == 0;
+    const View4 vk{nokv ? c.q : c.k, {c.D, nokv ? 1u : c.KS, nokv ? 1u : c.Hkv, nokv ? 1u : c.B},
+                   {c.ks[2], c.ks[1], c.ks[0]}};
+    const View4 vv{nokv ? c.q : c.v, {c.D, nokv ? 1u : c.KS, nokv ? 1u : c.Hkv, nokv ? 1u : c.B},
+                   {c.vs[2], c.vs[1], c.vs[0]}};
     const View4 vo{c.o, {c.D, c.S, c.H, c.B}, {c.os[2], c.os[1], c.os[0]}};
     const char* e = nullptr;
     if ((e = make_map(&tmQ, vq, dt, T::ESZ, T::BOX, BM, sw)) ||
@@ -167,6 +174,15 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
     auto kern = fa_prefill_kernel<T>;
     cudaError_t ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM_BYTES);
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
+    if constexpr (T::RESPLIT) {
+        // setmaxnreg.inc waits for registers the CTA was launched with: refuse to
+        // launch unless the binary really allocates LAUNCH_REGS per thread.
+        cudaFuncAttributes fa{};
+        ce = cudaFuncGetAttributes(&fa, kern);
+        if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
+        if (fa.numRegs != T::LAUNCH_REGS)
+            return fail(err, "internal: kernel register count does not match its register split");
+    }
     kern<<<static_cast<unsigned>(items), T::THREADS, T::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, tmO, p);
     ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
@@ -195,33 +211,83 @@ int dispatch_f16_dim(char* err, const Common& c, const prefill::Params& p, cudaS
 
 }  // namespace
 
-int forwardF16(const ForwardParams& a, void* stream) {
-    Common c{a.q, a.k, a.v, a.o,
-             {a.qStrideB, a.qStrideH, a.qStrideS}, {a.kStrideB, a.kStrideH, a.kStrideS},
-             {a.vStrideB, a.vStrideH, a.vStrideS}, {a.oStrideB, a.oStrideH, a.oStrideS},
-             a.batchSize, a.numHeads, a.numKvHeads, a.seqLen, a.keySeqLen, a.headDim, 2};
+namespace {
+
+constexpr size_t kWsAlign = 256;
+
+size_t align_up(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
+
+// Workspace of an FP16 call: rotated Q and K (contiguous fp16) when RoPE is on.
+size_t f16_workspace_bytes(const ForwardParams& a) {
+    if (!a.hasRope) return 0;
+    const size_t q = static_cast<size_t>(a.batchSize) * a.numHeads * a.seqLen * a.headDim * 2;
+    const size_t k = static_cast<size_t>(a.batchSize) * a.numKvHeads * a.keySeqLen * a.headDim * 2;
+    return align_up(q) + align_up(k);
+}
+
+int f16_validate(const Common& c, const ForwardParams& a) {
     if (const char* e = check_common(c)) return fail(g_err_f16, "%s", e);
     if (a.headDim < 32 || a.headDim > 512 || a.headDim % 32 != 0)
         return fail(g_err_f16, "unsupported head_dim (multiples of 32 from 32 to 512)");
     if (a.hasRope) {
-        if (a.rot_cos == nullptr || a.rot_sin == nullptr) return fail(g_err_f16, "has_rope set but rot_cos/rot_sin is null");
+        if (a.rot_cos == nullptr || a.rot_sin == nullptr)
+            return fail(g_err_f16, "has_rope set but rot_cos/rot_sin is null");
         if ((reinterpret_cast<uintptr_t>(a.rot_cos) & 15u) || (reinterpret_cast<uintptr_t>(a.rot_sin) & 15u))
             return fail(g_err_f16, "rot_cos/rot_sin must be 16-byte aligned");
     }
     if (a.seqLen > (1u << 30) || a.keySeqLen > (1u << 30)) return fail(g_err_f16, "sequence too long");
+    return 0;
+}
 
+Common f16_common(const ForwardParams& a) {
+    return Common{a.q, a.k, a.v, a.o,
+                  {a.qStrideB, a.qStrideH, a.qStrideS}, {a.kStrideB, a.kStrideH, a.kStrideS},
+                  {a.vStrideB, a.vStrideH, a.vStrideS}, {a.oStrideB, a.oStrideH, a.oStrideS},
+                  a.batchSize, a.numHeads, a.numKvHeads, a.seqLen, a.keySeqLen, a.headDim, 2};
+}
+
+// Enqueues the rotation of Q and K into `ws`; rewrites `c` to read the rotated copies.
+int launch_rope(const ForwardParams& a, Common& c, void* ws, cudaStream_t st) {
+    rope::Params rp{};
+    __half* qr = static_cast<__half*>(ws);
+    const size_t qbytes = static_cast<size_t>(a.batchSize) * a.numHeads * a.seqLen * a.headDim * 2;
+    __half* kr = reinterpret_cast<__half*>(static_cast<char*>(ws) + align_up(qbytes));
+    rp.t[0] = rope::Tensor4{static_cast<const __half*>(a.q), qr, a.qStrideB, a.qStrideH, a.qStrideS,
+                            static_cast<int>(a.batchSize), static_cast<int>(a.numHeads), static_cast<int>(a.seqLen)};
+    rp.t[1] = rope::Tensor4{static_cast<const __half*>(a.k), kr, a.kStrideB, a.kStrideH, a.kStrideS,
+                            static_cast<int>(a.batchSize), static_cast<int>(a.numKvHeads),
+                            static_cast<int>(a.keySeqLen)};
+    rp.chunks[0] = static_cast<int64_t>(a.batchSize) * a.numHeads * a.seqLen * (a.headDim / 8);
+    rp.chunks[1] = static_cast<int64_t>(a.batchSize) * a.numKvHeads * a.keySeqLen * (a.headDim / 8);
+    rp.cos_t = static_cast<const float*>(a.rot_cos);
+    rp.sin_t = static_cast<const float*>(a.rot_sin);
+    rp.D = static_cast<int>(a.headDim);
+    const int64_t total = rp.chunks[0] + rp.chunks[1];
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t want = (total + 255) / 256;
+    const int grid = static_cast<int>(want < static_cast<int64_t>(sms) * 8 ? want : static_cast<int64_t>(sms) * 8);
+    if (grid > 0) rope::rope_rotate_kernel<<<grid, 256, 0, st>>>(rp);
+    cudaError_t ce = cudaGetLastError();
+    if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    const int64_t D = a.headDim;
+    c.q = qr;
+    c.qs[0] = static_cast<int64_t>(a.numHeads) * a.seqLen * D;
+    c.qs[1] = static_cast<int64_t>(a.seqLen) * D;
+    c.qs[2] = D;
+    c.k = kr;
+    c.ks[0] = static_cast<int64_t>(a.numKvHeads) * a.keySeqLen * D;
+    c.ks[1] = static_cast<int64_t>(a.keySeqLen) * D;
+    c.ks[2] = D;
+    return 0;
+}
+
+int f16_attention(const ForwardParams& a, const Common& c, cudaStream_t st) {
     prefill::Params p{};
     p.causal = a.causal ? 1 : 0;
     p.window = a.windowSize > 0 ? a.windowSize : 0;
-    p.has_rope = a.hasRope ? 1 : 0;
     p.scale_log2 = a.scale * 1.4426950408889634f;
-    p.rot_cos = static_cast<const float*>(a.rot_cos);
-    p.rot_sin = static_cast<const float*>(a.rot_sin);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-
-    if (!a.hasRope && decode::eligible(a.seqLen, a.numHeads / a.numKvHeads, a.headDim))
-        return decode::launch_f16(g_err_f16, a, st);
-
     switch (a.headDim) {
 #define RDNA_D(Dv) \
     case Dv: return dispatch_f16_dim<Dv>(g_err_f16, c, p, st);
@@ -232,6 +298,139 @@ int forwardF16(const ForwardParams& a, void* stream) {
             break;
     }
     return fail(g_err_f16, "unsupported head_dim (multiples of 32 from 32 to 512)");
+}
+
+}  // namespace
+
+namespace decode {
+
+// Cluster-split decode launch: one cluster of CS CTAs per (batch, kv head).
+int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
+    const int D = static_cast<int>(a.headDim);
+    Params p{};
+    p.q = static_cast<const __half*>(a.q);
+    p.o = static_cast<__half*>(a.o);
+    p.qsb = a.qStrideB;
+    p.qsh = a.qStrideH;
+    p.qss = a.qStrideS;
+    p.osb = a.oStrideB;
+    p.osh = a.oStrideH;
+    p.oss = a.oStrideS;
+    p.B = static_cast<int>(a.batchSize);
+    p.H = static_cast<int>(a.numHeads);
+    p.Hkv = static_cast<int>(a.numKvHeads);
+    p.S = static_cast<int>(a.seqLen);
+    p.KS = static_cast<int>(a.keySeqLen);
+    p.G = p.H / p.Hkv;
+    p.R = p.G * p.S;
+    p.delta = p.KS - p.S;
+    p.causal = a.causal ? 1 : 0;
+    p.window = a.windowSize > 0 ? a.windowSize : 0;
+    p.scale_log2 = a.scale * 1.4426950408889634f;
+
+    CUtensorMap tmK, tmV;
+    const bool nokv = a.keySeqLen == 0;
+    const uint64_t e1 = nokv ? 1 : a.keySeqLen, e2 = nokv ? 1 : a.numKvHeads, e3 = nokv ? 1 : a.batchSize;
+    const View4 vk{nokv ? a.q : a.k, {a.headDim, e1, e2, e3}, {a.kStrideS, a.kStrideH, a.kStrideB}};
+    const View4 vv{nokv ? a.q : a.v, {a.headDim, e1, e2, e3}, {a.vStrideS, a.vStrideH, a.vStrideB}};
+    const char* e = nullptr;
+    if ((e = make_map(&tmK, vk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 64, KT, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (e = make_map(&tmV, vv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 64, KT, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return fail(err, "%s", e);
+
+    const int64_t units = static_cast<int64_t>(p.B) * p.Hkv;
+    if (units > 65535) return fail(err, "too many (batch, kv head) units for one decode launch");
+    const int64_t tiles = (static_cast<int64_t>(p.KS) + KT - 1) / KT;
+    // Cluster size: the smallest split (fewest CTAs, least combine work) whose
+    // waves over the SMs (one CTA each) are >= 95% full; each CTA keeps >= 8 tiles.
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto wave_eff = [&](int c) {
+        const int64_t ctas = units * c;
+        const int64_t waves = (ctas + sms - 1) / sms;
+        return static_cast<double>(ctas) / static_cast<double>(waves * sms);
+    };
+    int cs = 1;
+    double best = wave_eff(1);
+    for (int c = 2; c <= MAX_CLUSTER && tiles / c >= 8; c *= 2) {
+        if (best >= 0.95) break;
+        if (wave_eff(c) > best + 1e-9) {
+            best = wave_eff(c);
+            cs = c;
+        }
+    }
+
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(cs, static_cast<unsigned>(units), 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t ce;
+    if (D == 64) {
+        cfg.dynamicSmemBytes = Layout<64>::SMEM_BYTES;
+        ce = cudaFuncSetAttribute(fa_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Layout<64>::SMEM_BYTES);
+        if (ce == cudaSuccess) ce = cudaLaunchKernelEx(&cfg, fa_decode_kernel<64>, tmK, tmV, p);
+    } else {
+        cfg.dynamicSmemBytes = Layout<128>::SMEM_BYTES;
+        ce = cudaFuncSetAttribute(fa_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Layout<128>::SMEM_BYTES);
+        if (ce == cudaSuccess) ce = cudaLaunchKernelEx(&cfg, fa_decode_kernel<128>, tmK, tmV, p);
+    }
+    if (ce == cudaSuccess) ce = cudaGetLastError();
+    if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
+    return 0;
+}
+
+}  // namespace decode
+
+namespace {
+}  // namespace
+
+size_t workspaceBytesF16(const ForwardParams& a) { return f16_workspace_bytes(a); }
+
+int forwardF16Ws(const ForwardParams& a, void* workspace, size_t workspace_bytes, void* stream) {
+    Common c = f16_common(a);
+    if (int rc = f16_validate(c, a)) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t need = f16_workspace_bytes(a);
+    if (need > 0) {
+        if (workspace == nullptr || workspace_bytes < need)
+            return fail(g_err_f16, "workspace missing or smaller than rdna_attention_forward_workspace_size()");
+        if (reinterpret_cast<uintptr_t>(workspace) & (kWsAlign - 1))
+            return fail(g_err_f16, "workspace must be 256-byte aligned");
+        if (int rc = launch_rope(a, c, workspace, st)) return rc;
+    } else if (decode::eligible(a.seqLen, a.numHeads / a.numKvHeads, a.headDim)) {
+        return decode::launch_f16(g_err_f16, a, st);
+    }
+    return f16_attention(a, c, st);
+}
+
+int forwardF16(const ForwardParams& a, void* stream) {
+    const size_t need = f16_workspace_bytes(a);
+    if (need == 0) return forwardF16Ws(a, nullptr, 0, stream);
+    {
+        Common c = f16_common(a);
+        if (int rc = f16_validate(c, a)) return rc;
+    }
+    // Stream-ordered workspace for the rotated Q/K: allocated and released on
+    // the caller's stream, so the call still never blocks the host.
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    void* ws = nullptr;
+    cudaError_t ce = cudaMallocAsync(&ws, need, st);
+    if (ce != cudaSuccess) return fail(g_err_f16, "workspace allocation failed: %s", cudaGetErrorString(ce));
+    const int rc = forwardF16Ws(a, ws, need, stream);
+    ce = cudaFreeAsync(ws, st);
+    if (rc != 0) return rc;
+    if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    return 0;
 }
 
 int forwardInt8QK(const ForwardParamsInt8QK& a, void* stream) {
@@ -249,7 +448,6 @@ int forwardInt8QK(const ForwardParamsInt8QK& a, void* stream) {
     prefill::Params p{};
     p.causal = a.causal ? 1 : 0;
     p.window = a.windowSize > 0 ? a.windowSize : 0;
-    p.has_rope = 0;
     p.scale_log2 = a.scale * 1.4426950408889634f;
     p.q_scale = a.qScale;
     p.k_scale = a.kScale;

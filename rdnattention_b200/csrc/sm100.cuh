@@ -235,6 +235,18 @@ __host__ __device__ constexpr uint32_t instr_desc(uint32_t c_fmt, uint32_t ab_fm
            ((M >> 4) << 24);
 }
 
+// Register re-split between warpgroups.  Must be executed by all four warps
+// of a warpgroup; the sum over the CTA may not exceed the registers it was
+// launched with (threads x registers per thread at launch).
+template <int N>
+RDNA_DEV void regs_increase() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+RDNA_DEV void regs_decrease() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // --------------------------------------------------------------- math utils
 
 RDNA_DEV float ex2(float x) {
