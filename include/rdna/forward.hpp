@@ -68,6 +68,11 @@ size_t workspaceBytesF16(const ForwardParams& params);
 /// forwardF16 with a caller-provided workspace (256-byte aligned, at least
 /// workspaceBytesF16() bytes; may be null when that is 0).  Allocates nothing.
 int forwardF16Ws(const ForwardParams& params, void* workspace, size_t workspace_bytes, void* stream);
+/// forwardF16 taking its RoPE workspace from a fixed 32 MiB device array
+/// inside the library instead of allocating (see rdna_attention_forward_noalloc).
+int forwardF16NoAlloc(const ForwardParams& params, void* stream);
+/// Size of that fixed array in bytes.
+size_t noAllocWorkspaceLimit();
 /// Reason the most recent forwardF16() call on this thread failed, or nullptr.
 const char* lastError();
 /// Enqueues the INT8 forward on `stream`. Non-blocking. 0 on success.

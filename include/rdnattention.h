@@ -108,6 +108,39 @@ RDNA_API int32_t rdna_attention_forward_ws(
     float scale, int32_t causal, int32_t has_rope, int32_t window_size,
     void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* FP16 forward that allocates nothing, even with RoPE.  No counterpart in
+ * the reference library.
+ *
+ * Who needs it: callers that cannot allocate device memory — a plugin
+ * running inside a host framework that owns the device allocator and
+ * forbids allocations behind its back, a process under a hard device-memory
+ * budget where an allocation may fail at any time, or a device without
+ * stream-ordered memory pools (where rdna_attention_forward's cudaMallocAsync
+ * is unavailable).  Same arguments and return codes as
+ * rdna_attention_forward.
+ *
+ * The RoPE workspace (rotated Q and K, fp16, each rounded up to 256 bytes)
+ * lives in a fixed 32 MiB array inside the library, which every GPU that
+ * loads the library keeps reserved until the process exits; a problem whose
+ * workspace exceeds it (for example batch 1, 32 heads / 8 KV heads, 2048
+ * tokens, head_dim 128 fits; 4096 tokens does not) returns -3 with a message
+ * naming the limit.  Without RoPE no workspace is used.  The first call on a
+ * device looks up the array's device address on that device; make that
+ * first call before any stream capture.  All calls share the one array:
+ * calls that overlap on the GPU (different streams or threads) race on it,
+ * so serialise them. */
+RDNA_API int32_t rdna_attention_forward_noalloc(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* stream);
+
 /* Reads and clears the device status word of the current device: out[0] =
  * first error code a kernel recorded (a bounded wait that expired), out[1] =
  * number of such events.  Synchronises the current device.  Returns 0, or

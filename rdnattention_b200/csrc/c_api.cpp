@@ -182,6 +182,28 @@ RDNA_API int32_t rdna_attention_forward_int8qk(
     return 0;
 }
 
+RDNA_API int32_t rdna_attention_forward_noalloc(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* stream) {
+    const rdna::ForwardParams p = f16_params(q, k, v, output, rot_cos, rot_sin, q_stride_b, q_stride_h, q_stride_s,
+                                             k_stride_b, k_stride_h, k_stride_s, v_stride_b, v_stride_h, v_stride_s,
+                                             o_stride_b, o_stride_h, o_stride_s, batch_size, num_heads, num_kv_heads,
+                                             seq_len, key_seq_len, head_dim, scale, causal, has_rope, window_size);
+    if (rdna::forwardF16NoAlloc(p, stream) != 0) {
+        set_error("Attention (fp16) failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
 RDNA_API int32_t rdna_debug_read_status(int32_t* out2) {
     const char* why = nullptr;
     if (out2 == nullptr) {

@@ -433,6 +433,55 @@ int forwardF16(const ForwardParams& a, void* stream) {
     return 0;
 }
 
+// ------------------------------------------------- fixed-workspace variant
+//
+// For callers that cannot allocate device memory (see
+// rdna_attention_forward_noalloc in rdnattention.h): the RoPE workspace is this
+// file-scope array, reserved on every device that loads the library's module
+// until the process exits.  In host code the name below is only a host-side
+// stand-in; its device address comes from cudaGetSymbolAddress, taken once
+// per device with that device current, on the first call there.  Every call
+// shares the array: the RoPE pre-pass overwrites every byte the attention
+// kernel reads before it is read, so nothing needs clearing, but calls that
+// overlap on the GPU (other streams, other threads) race on it.
+constexpr size_t kNoAllocWorkspaceBytes = size_t(32) << 20;  // 32 MiB
+static __device__ __align__(256) unsigned char g_noalloc_workspace[kNoAllocWorkspaceBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+constexpr int kMaxDevices = 256;
+void* g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+size_t noAllocWorkspaceLimit() { return kNoAllocWorkspaceBytes; }
+
+int forwardF16NoAlloc(const ForwardParams& a, void* stream) {
+    const size_t need = f16_workspace_bytes(a);
+    if (need > kNoAllocWorkspaceBytes) {
+        char msg[160];
+        std::snprintf(msg, sizeof(msg), "RoPE workspace of %zu bytes exceeds the fixed %zu-byte no-alloc workspace",
+                      need, kNoAllocWorkspaceBytes);
+        return fail(g_err_f16, "%s", msg);
+    }
+    if (need == 0) return forwardF16Ws(a, nullptr, 0, stream);
+    int dev = -1;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    if (dev < 0 || dev >= kMaxDevices) return fail(g_err_f16, "device ordinal out of range");
+    void* ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (g_noalloc_ptr[dev] == nullptr) {
+            void* p = nullptr;
+            ce = cudaGetSymbolAddress(&p, g_noalloc_workspace);
+            if (ce != cudaSuccess) return fail(g_err_f16, "cudaGetSymbolAddress: %s", cudaGetErrorString(ce));
+            g_noalloc_ptr[dev] = p;
+        }
+        ws = g_noalloc_ptr[dev];
+    }
+    return forwardF16Ws(a, ws, kNoAllocWorkspaceBytes, stream);
+}
+
 int forwardInt8QK(const ForwardParamsInt8QK& a, void* stream) {
     Common c{a.q, a.k, a.v, a.o,
              {a.qStrideB, a.qStrideH, a.qStrideS}, {a.kStrideB, a.kStrideH, a.kStrideS},
