@@ -278,10 +278,21 @@ __device__ __forceinline__ void load_s_row(uint32_t taddr, uint32_t* r) {
     }
 }
 
-// lround(x) for x >= 0, exactly (round half away from zero).
-__device__ __forceinline__ int lround_pos(float x) {
-    const float t = truncf(x);
-    return static_cast<int>(t) + ((x - t) >= 0.5f ? 1 : 0);
+
+// Row max of N values with 8 independent chains of 3-input max (dependency
+// depth ~N/16 instead of N).
+template <int N>
+__device__ __forceinline__ float row_max(const float* x) {
+    static_assert(N % 16 == 0, "row length");
+    float m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = fmaxf(x[i], x[i + 8]);
+#pragma unroll
+    for (int c = 16; c < N; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m[i] = fmax3(m[i], x[c + i], x[c + 8 + i]);
+    }
+    return fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
 // Warp-uniform bounded wait: every lane of the warp gets the same answer, so
@@ -362,22 +373,25 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         const bool full = block_full<T>(p, row0, j);
         const int lo = klo - j * T::BC, hi = khi - j * T::BC;
 
-        float mx = -INFINITY;
+        float mx;
         if constexpr (T::I8) {
+            // s32 -> float on the ALU (exact: |q.k| <= 127*127*D < 2^22), scaled into the
+            // log2 domain: x = float(acc) * q_scale * k_scale * scale * log2(e)
             const float* ksb = ksbuf + (it & 1) * T::BC;
+            if (kvec) {
 #pragma unroll
-            for (int c = 0; c < T::BC; ++c) {
-                float v = static_cast<float>(static_cast<int>(raw[c])) * rowscale;
-                if (kvec) v *= ksb[c];
-                x[c] = v;
+                for (int c = 0; c < T::BC; ++c) x[c] = (i2f_biased(raw[c]) - 12582912.0f) * ksb[c] * rowscale;
+            } else {
+                const float bias = -12582912.0f * rowscale;
+#pragma unroll
+                for (int c = 0; c < T::BC; ++c) x[c] = fmaf(i2f_biased(raw[c]), rowscale, bias);
             }
             if (!full) {
 #pragma unroll
                 for (int c = 0; c < T::BC; ++c)
                     if (c < lo || c > hi) x[c] = -INFINITY;
             }
-#pragma unroll
-            for (int c = 0; c < T::BC; ++c) mx = fmaxf(mx, x[c]);
+            mx = row_max<T::BC>(x);
         } else {
             if (sl2 > 0.f) {
                 if (!full) {
@@ -385,9 +399,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
                     for (int c = 0; c < T::BC; ++c)
                         if (c < lo || c > hi) x[c] = -INFINITY;
                 }
-#pragma unroll
-                for (int c = 0; c < T::BC; ++c) mx = fmaxf(mx, x[c]);
-                mx *= sl2;
+                mx = row_max<T::BC>(x) * sl2;
             } else {
                 // non-positive scale: scale first, then mask (rare; keeps max semantics exact)
 #pragma unroll
@@ -395,8 +407,8 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
                     float v = x[c] * sl2;
                     if (!full && (c < lo || c > hi)) v = -INFINITY;
                     x[c] = v;
-                    mx = fmaxf(mx, v);
                 }
+                mx = row_max<T::BC>(x);
             }
         }
 
@@ -456,7 +468,9 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
         float lsum = 0.f;
         // P goes back over S in 32-key chunks (S is already in registers), so only
-        // one chunk of packed P is live at a time.
+        // one chunk of packed P is live at a time.  8 independent partial sums keep
+        // the row-sum dependency chain short.
+        float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if constexpr (!T::I8) {
             const float mul = (sl2 > 0.f) ? sl2 : 1.f;
 #pragma unroll
@@ -464,32 +478,38 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
                 uint32_t pk[16];
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
-                    const float p0 = ex2(fmaf(x[c0 + c], mul, neg_m));
-                    const float p1 = ex2(fmaf(x[c0 + c + 1], mul, neg_m));
-                    lsum += p0 + p1;
+                    const float a0 = fmaf(x[c0 + c], mul, neg_m);
+                    const float a1 = fmaf(x[c0 + c + 1], mul, neg_m);
+                    // all exponentials on the MUFU: moving a share to the FMA pipe
+                    // (exp2_fma) measured slower here, the softmax is issue-bound
+                    const float p0 = ex2(a0);
+                    const float p1 = ex2(a1);
+                    ls[(c >> 1) & 7] += p0 + p1;
                     pk[c / 2] = pack_half2(p0, p1);
                 }
                 tmem_st_x16(tS + c0 / 2, pk);
             }
         } else {
+            // p in [0, 1] against the running max; quantised as round(p * 127) with the
+            // round-to-nearest of a 1.5*2^23 bias (same as lround except at exact .5 ties)
 #pragma unroll
             for (int c0 = 0; c0 < T::BC; c0 += 32) {
                 uint32_t pk[8];
 #pragma unroll
                 for (int c = 0; c < 32; c += 4) {
-                    uint32_t word = 0;
+                    uint32_t qb[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const float pv = ex2(x[c0 + c + i] + neg_m);
-                        lsum += pv;
-                        const int qv = min(127, lround_pos(pv * 127.f));
-                        word |= static_cast<uint32_t>(qv) << (8 * i);
+                        ls[((c >> 2) + i) & 7] += pv;
+                        qb[i] = static_cast<uint32_t>(__float_as_int(fmaf(pv, 127.0f, 12582912.0f)));
                     }
-                    pk[c / 4] = word;
+                    pk[c / 4] = pack_low_bytes(qb[0], qb[1], qb[2], qb[3]);
                 }
                 tmem_st_x8(tS + c0 / 4, pk);
             }
         }
+        lsum = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         l += lsum;
         tmem_wait_st();
         tc_fence_before();

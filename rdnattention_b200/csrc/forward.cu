@@ -183,6 +183,7 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
         if (fa.numRegs != T::LAUNCH_REGS)
             return fail(err, "internal: kernel register count does not match its register split");
     }
+
     kern<<<static_cast<unsigned>(items), T::THREADS, T::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, tmO, p);
     ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
@@ -257,18 +258,23 @@ int launch_rope(const ForwardParams& a, Common& c, void* ws, cudaStream_t st) {
     rp.t[1] = rope::Tensor4{static_cast<const __half*>(a.k), kr, a.kStrideB, a.kStrideH, a.kStrideS,
                             static_cast<int>(a.batchSize), static_cast<int>(a.numKvHeads),
                             static_cast<int>(a.keySeqLen)};
-    rp.chunks[0] = static_cast<int64_t>(a.batchSize) * a.numHeads * a.seqLen * (a.headDim / 8);
-    rp.chunks[1] = static_cast<int64_t>(a.batchSize) * a.numKvHeads * a.keySeqLen * (a.headDim / 8);
+    const int64_t qrows = static_cast<int64_t>(a.batchSize) * a.numHeads * a.seqLen;
+    const int64_t krows = static_cast<int64_t>(a.batchSize) * a.numKvHeads * a.keySeqLen;
+    if (qrows + krows > INT32_MAX) return fail(g_err_f16, "RoPE pre-pass: too many rows for one launch");
+    rp.rows[0] = static_cast<int>(qrows);
+    rp.rows[1] = static_cast<int>(krows);
     rp.cos_t = static_cast<const float*>(a.rot_cos);
     rp.sin_t = static_cast<const float*>(a.rot_sin);
     rp.D = static_cast<int>(a.headDim);
-    const int64_t total = rp.chunks[0] + rp.chunks[1];
+    rp.cpr = rp.D / 8;
+    rp.rpb = 256 / rp.cpr;
+    const int64_t total = qrows + krows;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t want = (total + 255) / 256;
+    const int64_t want = (total + rp.rpb - 1) / rp.rpb;
     const int grid = static_cast<int>(want < static_cast<int64_t>(sms) * 8 ? want : static_cast<int64_t>(sms) * 8);
-    if (grid > 0) rope::rope_rotate_kernel<<<grid, 256, 0, st>>>(rp);
+    if (grid > 0) rope::rope_rotate_kernel<<<grid, rp.rpb * rp.cpr, 0, st>>>(rp);
     cudaError_t ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
     const int64_t D = a.headDim;

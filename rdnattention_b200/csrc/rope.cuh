@@ -27,27 +27,30 @@ struct Tensor4 {
 };
 
 struct Params {
-    Tensor4 t[2];        // Q, K
-    int64_t chunks[2];   // 16-byte chunks per tensor
+    Tensor4 t[2];    // Q, K
+    int rows[2];     // B * H * S rows per tensor
     const float* cos_t;
     const float* sin_t;
     int D;
+    int cpr;         // 16-byte chunks per row (D / 8)
+    int rpb;         // rows per block iteration (blockDim.x / cpr)
 };
 
+// blockDim.x = rpb * cpr: thread -> (row within the block's slab, chunk).
+// Index math is per row and 32-bit (rows < 2^31).
 __global__ void __launch_bounds__(256) rope_rotate_kernel(const __grid_constant__ Params p) {
-    const int cpr = p.D / 8;  // chunks per row
-    const int64_t total = p.chunks[0] + p.chunks[1];
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int which = i < p.chunks[0] ? 0 : 1;
+    const int ch = threadIdx.x % p.cpr;
+    const int rsub = threadIdx.x / p.cpr;
+    if (rsub >= p.rpb) return;
+    const int total = p.rows[0] + p.rows[1];
+    for (int row = blockIdx.x * p.rpb + rsub; row < total; row += gridDim.x * p.rpb) {
+        const int which = row < p.rows[0] ? 0 : 1;
         const Tensor4& T = p.t[which];
-        const int64_t c = which == 0 ? i : i - p.chunks[0];
-        const int ch = static_cast<int>(c % cpr);
-        const int64_t row = c / cpr;  // (b * H + h) * S + s
-        const int s = static_cast<int>(row % T.S);
-        const int64_t bh = row / T.S;
-        const int h = static_cast<int>(bh % T.H);
-        const int b = static_cast<int>(bh / T.H);
+        const unsigned r = static_cast<unsigned>(which == 0 ? row : row - p.rows[0]);
+        const unsigned s = r % static_cast<unsigned>(T.S);
+        const unsigned bh = r / static_cast<unsigned>(T.S);
+        const unsigned h = bh % static_cast<unsigned>(T.H);
+        const unsigned b = bh / static_cast<unsigned>(T.H);
         const uint4 x = *reinterpret_cast<const uint4*>(T.src + b * T.sb + h * T.sh + s * T.ss + ch * 8);
         const int64_t toff = static_cast<int64_t>(s) * (p.D / 2) + ch * 4;
         const float4 cv = __ldg(reinterpret_cast<const float4*>(p.cos_t + toff));
@@ -61,10 +64,10 @@ __global__ void __launch_bounds__(256) rope_rotate_kernel(const __grid_constant_
         for (int k = 0; k < 4; ++k) {
             const __half2 h2 = *reinterpret_cast<const __half2*>(&u[k]);
             const float a = __low2float(h2), bb = __high2float(h2);
-            const __half2 r = __floats2half2_rn(a * cc[k] - bb * ss[k], a * ss[k] + bb * cc[k]);
-            w[k] = *reinterpret_cast<const uint32_t*>(&r);
+            const __half2 rr = __floats2half2_rn(a * cc[k] - bb * ss[k], a * ss[k] + bb * cc[k]);
+            w[k] = *reinterpret_cast<const uint32_t*>(&rr);
         }
-        *reinterpret_cast<uint4*>(T.dst + row * p.D + ch * 8) = y;
+        *reinterpret_cast<uint4*>(T.dst + static_cast<int64_t>(r) * p.D + ch * 8) = y;
     }
 }
 

@@ -255,6 +255,48 @@ RDNA_DEV float ex2(float x) {
     return y;
 }
 
+// Three-input max (sm_100).
+RDNA_DEV float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^x on the FMA/ALU pipes, for x <= 8 (softmax arguments), leaving the MUFU
+// free for the other exponentials.  Cody-Waite split x = n + f with
+// n = round(x) taken from the low mantissa bits of x + 1.5*2^23, f in
+// [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted for
+// this library (iteratively reweighted least squares for minimax relative
+// error on [-0.5, 0.5]: max relative error 7.5e-5, below fp16's 2^-11); 2^n by
+// adding n to the exponent field.  The polynomial lies in [0.7, 1.42]
+// (exponent field 126 or 127), so clamping x at -126 keeps the biased exponent
+// >= 0: arguments below -126 (masked keys, -inf) give ~1e-38, not a wrapped
+// exponent.
+RDNA_DEV float exp2_fma(float x) {
+    x = fmaxf(x, -126.0f);
+    const float t = x + 12582912.0f;
+    const float n = t - 12582912.0f;
+    const float f = x - n;
+    float p = fmaf(0.0551716685295105f, f, 0.2426111400127411f);
+    p = fmaf(p, f, 0.6932609677314758f);
+    p = fmaf(p, f, 0.9999280571937561f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Exact int32 -> float for |v| < 2^22 on the ALU/FMA pipes (avoids the
+// conversion unit, which shares throughput with the MUFU): returns
+// float(v) + 12582912.
+RDNA_DEV float i2f_biased(uint32_t v) { return __int_as_float(static_cast<int>(v + 0x4B400000u)); }
+
+// Bytes 0 of four words packed into one word (b0 lowest).
+RDNA_DEV uint32_t pack_low_bytes(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
+    uint32_t lo, hi, r;
+    asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(lo) : "r"(b0), "r"(b1));
+    asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(hi) : "r"(b2), "r"(b3));
+    asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+
 RDNA_DEV uint32_t pack_half2(float lo, float hi) {
     uint32_t r;
     // cvt.rn.f16x2.f32 d, a, b puts a in the upper half and b in the lower half.
