@@ -347,18 +347,24 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         ksbuf = reinterpret_cast<float*>(smem + 1024) + t * 2 * T::BC;
     }
 
+    // per-key K scales of the next block are fetched one block ahead, so the
+    // global-load latency never sits on the softmax critical path
+    const float* kvec_row = kvec ? p.k_vec + (static_cast<int64_t>(w.b) * p.Hkv + w.kvh) * p.KS : nullptr;
+    auto load_ks = [&](int jb) {
+        const int key = jb * T::BC + r;
+        return (kvec && r < T::BC && jb < e && key < p.KS) ? __ldg(kvec_row + key) : 0.f;
+    };
+    float ks_next = load_ks(a);
+
     int it = 0;
     for (int j = a; j < e; ++j, ++it) {
         if constexpr (T::I8) {
             if (kvec) {
                 // stage this block's per-key scales; buffer (it & 1) is reused every second block
                 const int buf = it & 1;
-                if (r < T::BC) {
-                    const int key = j * T::BC + r;
-                    ksbuf[buf * T::BC + r] =
-                        key < p.KS ? p.k_vec[(static_cast<int64_t>(w.b) * p.Hkv + w.kvh) * p.KS + key] : 0.f;
-                }
+                if (r < T::BC) ksbuf[buf * T::BC + r] = ks_next;
                 mbar_arrive(bar(Bars::KS_FULL + 2 * t + buf));
+                ks_next = load_ks(j + 1);
                 if (!aborted && !warp_wait(bar(Bars::KS_FULL + 2 * t + buf), (it >> 1) & 1, ab, SITE_SM_KS))
                     aborted = true;
             }
@@ -375,23 +381,31 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
 
         float mx;
         if constexpr (T::I8) {
-            // s32 -> float on the ALU (exact: |q.k| <= 127*127*D < 2^22), scaled into the
-            // log2 domain: x = float(acc) * q_scale * k_scale * scale * log2(e)
+            // s32 -> float on the ALU (exact: |q.k| <= 127*127*D < 2^22).  x holds
+            // float(acc) * k_scale; the per-row q_scale * scale * log2(e) (rowscale) is
+            // applied to the max and folded into the exponent's FMA below.
             const float* ksb = ksbuf + (it & 1) * T::BC;
             if (kvec) {
 #pragma unroll
-                for (int c = 0; c < T::BC; ++c) x[c] = (i2f_biased(raw[c]) - 12582912.0f) * ksb[c] * rowscale;
+                for (int c = 0; c < T::BC; ++c) x[c] = (i2f_biased(raw[c]) - 12582912.0f) * ksb[c];
             } else {
-                const float bias = -12582912.0f * rowscale;
 #pragma unroll
-                for (int c = 0; c < T::BC; ++c) x[c] = fmaf(i2f_biased(raw[c]), rowscale, bias);
+                for (int c = 0; c < T::BC; ++c) x[c] = i2f_biased(raw[c]) - 12582912.0f;
             }
             if (!full) {
 #pragma unroll
                 for (int c = 0; c < T::BC; ++c)
-                    if (c < lo || c > hi) x[c] = -INFINITY;
+                    if (c < lo || c > hi) x[c] = rowscale >= 0.f ? -INFINITY : INFINITY;
             }
-            mx = row_max<T::BC>(x);
+            // max of x * rowscale: max(x) * rowscale for rowscale >= 0, else min(x) * rowscale
+            if (rowscale >= 0.f) {
+                mx = row_max<T::BC>(x) * rowscale;
+            } else {
+#pragma unroll
+                for (int c = 0; c < T::BC; ++c) x[c] = -x[c];
+                mx = row_max<T::BC>(x) * -rowscale;
+            }
+            if (mx != mx) mx = -INFINITY;  // fully masked row with rowscale == 0
         } else {
             if (sl2 > 0.f) {
                 if (!full) {
@@ -441,6 +455,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
             const bool flush = rescale || (it > 0 && since_flush >= 512);
             if (__any_sync(0xffffffffu, flush)) {
                 const float c = rescale ? corr : 1.f;
+                const float ps = p.pv_scale;
                 for (int c0 = 0; c0 < dv; c0 += 32) {
                     uint32_t acc[32], o[32];
                     tmem_ld_x32(tACC + c0, acc);
@@ -448,8 +463,8 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const float of = oflushed ? __uint_as_float(o[i]) : 0.f;
-                        const float nv = (of + static_cast<float>(static_cast<int>(acc[i])) * p.pv_scale) * c;
-                        o[i] = flush ? __float_as_uint(nv) : o[i];
+                        const float af = i2f_biased(acc[i]) - 12582912.0f;  // |acc| < 2^22 between flushes
+                        o[i] = flush ? __float_as_uint(fmaf(af, ps, of) * c) : o[i];
                         acc[i] = flush ? 0u : acc[i];
                     }
                     tmem_st_x32(tO + c0, o);
@@ -490,23 +505,32 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
                 tmem_st_x16(tS + c0 / 2, pk);
             }
         } else {
-            // p in [0, 1] against the running max; quantised as round(p * 127) with the
-            // round-to-nearest of a 1.5*2^23 bias (same as lround except at exact .5 ties)
+            // p in [0, 1] against the running max, computed two at a time in half
+            // precision (P only keeps 7 bits): fma(p, 127, 1024) in fp16 has unit
+            // spacing, so its low byte is round(p * 127) (round-to-nearest-even; the
+            // reference's lround differs only at exact .5 ties).  Row sums accumulate
+            // in 8 f16x2 partials (<= 8 values each) and finish in fp32.
+            const float ars = fabsf(rowscale);       // x was negated when rowscale < 0
+            constexpr uint32_t k127 = 0x57F057F0u;   // (127, 127) in f16x2
+            constexpr uint32_t k1024 = 0x64006400u;  // (1024, 1024)
+            uint32_t hs[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll
             for (int c0 = 0; c0 < T::BC; c0 += 32) {
                 uint32_t pk[8];
 #pragma unroll
                 for (int c = 0; c < 32; c += 4) {
-                    uint32_t qb[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float pv = ex2(x[c0 + c + i] + neg_m);
-                        ls[((c >> 2) + i) & 7] += pv;
-                        qb[i] = static_cast<uint32_t>(__float_as_int(fmaf(pv, 127.0f, 12582912.0f)));
-                    }
-                    pk[c / 4] = pack_low_bytes(qb[0], qb[1], qb[2], qb[3]);
+                    const uint32_t e0 = ex2_h2(pack_half2(fmaf(x[c0 + c], ars, neg_m), fmaf(x[c0 + c + 1], ars, neg_m)));
+                    const uint32_t e1 =
+                        ex2_h2(pack_half2(fmaf(x[c0 + c + 2], ars, neg_m), fmaf(x[c0 + c + 3], ars, neg_m)));
+                    hs[(c >> 2) & 7] = hadd2(hs[(c >> 2) & 7], hadd2(e0, e1));
+                    pk[c / 4] = pack_half_low_bytes(hfma2(e0, k127, k1024), hfma2(e1, k127, k1024));
                 }
                 tmem_st_x8(tS + c0 / 4, pk);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const __half2 h = *reinterpret_cast<const __half2*>(&hs[i]);
+                ls[i] = __low2float(h) + __high2float(h);
             }
         }
         lsum = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));

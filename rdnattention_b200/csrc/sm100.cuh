@@ -297,6 +297,29 @@ RDNA_DEV uint32_t pack_low_bytes(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t
     return r;
 }
 
+// Packed half-precision helpers.
+RDNA_DEV uint32_t ex2_h2(uint32_t x) {
+    uint32_t y;
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+RDNA_DEV uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+RDNA_DEV uint32_t hadd2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// Byte 0 and byte 2 of a, then of b: the low bytes of the four halves.
+RDNA_DEV uint32_t pack_half_low_bytes(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, 0x6420;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
 RDNA_DEV uint32_t pack_half2(float lo, float hi) {
     uint32_t r;
     // cvt.rn.f16x2.f32 d, a, b puts a in the upper half and b in the lower half.
