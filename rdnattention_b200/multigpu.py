@@ -1,0 +1,97 @@
+"""(batch, KV-head group) sharding of the forward across the GPUs of one node.
+
+The units of work — a batch element together with one KV head and the G
+query heads that read it — are independent, so each rank computes its own
+units with no inter-GPU traffic inside the kernel, and one collective
+all-gather assembles the full output O on every rank (NCCL over NVLink on
+the GPU path).  Shards are strided views of the full tensors (base-pointer
+offsets, original strides), so nothing is repacked.
+
+The reference library is single-device; this module is the multi-GPU layer
+the B200 build adds around its C ABI.
+"""
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass(frozen=True)
+class Shard:
+    """The rectangular block of units a rank owns: batches [b0, b1) x KV heads [g0, g1)."""
+    axis: str  # "batch" or "kv_head"
+    b0: int
+    b1: int
+    g0: int
+    g1: int
+
+
+def _split(n: int, world: int, rank: int):
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def plan(batch: int, kv_heads: int, world: int, rank: int) -> Shard:
+    """Batch-major when every rank gets whole batch elements (batch >= world), else
+    split the KV-head groups (batch < world).  Uneven counts give the first ranks
+    one more unit; a rank may own nothing when units < world."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    if batch >= world or kv_heads < world:
+        b0, b1 = _split(batch, world, rank)
+        return Shard("batch", b0, b1, 0, kv_heads)
+    g0, g1 = _split(kv_heads, world, rank)
+    return Shard("kv_head", 0, batch, g0, g1)
+
+
+def local_views(q, k, v, shard: Shard):
+    """Strided views of the rank's units (no copies)."""
+    G = q.shape[1] // k.shape[1]
+    qs = q[shard.b0:shard.b1, shard.g0 * G:shard.g1 * G]
+    ks = k[shard.b0:shard.b1, shard.g0:shard.g1]
+    vs = v[shard.b0:shard.b1, shard.g0:shard.g1]
+    return qs, ks, vs
+
+
+def _default_compute(q, k, v, **kw):
+    from . import flash_attn_strided
+
+    return flash_attn_strided(q, k, v, **kw)
+
+
+def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: int = -1, rot_cos=None,
+                       rot_sin=None, group=None, compute: Optional[Callable] = None):
+    """Forward attention over all ranks of `group`: every rank passes the same full
+    [B, H, S, D] / [B, Hkv, KS, D] inputs, computes only its (batch, KV-head) units
+    and receives the full output.  `compute` replaces the local kernel call
+    (default: the sm_100a path through the C ABI)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    B, H, S, D = query.shape
+    Hkv = key.shape[1]
+    G = H // Hkv
+    compute = compute or _default_compute
+    shards = [plan(B, Hkv, world, r) for r in range(world)]
+    mine = shards[rank]
+    qs, ks, vs = local_views(query, key, value, mine)
+
+    # every rank contributes the same number of elements: pad to the largest shard
+    sizes = [(s.b1 - s.b0) * (s.g1 - s.g0) * G * S * D for s in shards]
+    cap = max(sizes)
+    send = torch.zeros(cap, dtype=query.dtype, device=query.device)
+    if sizes[rank] > 0:
+        o_local = compute(qs, ks, vs, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
+                          rot_sin=rot_sin)
+        send[:sizes[rank]] = o_local.reshape(-1)
+    recv = torch.empty(world * cap, dtype=query.dtype, device=query.device)
+    dist.all_gather_into_tensor(recv, send, group=group)
+
+    out = torch.empty(B, H, S, D, dtype=query.dtype, device=query.device)
+    for r, s in enumerate(shards):
+        if sizes[r] == 0:
+            continue
+        block = recv[r * cap:r * cap + sizes[r]].view(s.b1 - s.b0, (s.g1 - s.g0) * G, S, D)
+        out[s.b0:s.b1, s.g0 * G:s.g1 * G] = block
+    return out
