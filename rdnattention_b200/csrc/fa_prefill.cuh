@@ -98,8 +98,8 @@ struct Traits {
     // Register split (NT = 2 only): launched at LAUNCH_REGS per thread.
     static constexpr bool RESPLIT = NT == 2;
     static constexpr int LAUNCH_REGS = 168;
-    static constexpr int SOFTMAX_REGS = 200;
-    static constexpr int CONTROL_REGS = 80;
+    static constexpr int SOFTMAX_REGS = 216;
+    static constexpr int CONTROL_REGS = 56;
     static_assert(!RESPLIT || 256 * SOFTMAX_REGS + 128 * CONTROL_REGS <= THREADS * LAUNCH_REGS,
                   "register split exceeds the launch allocation");
 
