@@ -151,7 +151,8 @@ struct Bars {
     static constexpr int O_FULL = 48;     // +NT
     static constexpr int KS_FULL = 50;    // +2*NT (INT8 per-key scale handoff, by block parity)
     static constexpr int EPI = 54;        // +NT (O staging written)
-    static constexpr int COUNT = 56;
+    static constexpr int EXPD = 56;       // +NT (softmax exp phase finished, one arrive per warp)
+    static constexpr int COUNT = 58;
     static constexpr int TMEM_SLOT = COUNT * 8;      // u32 TMEM base
     static constexpr int ABORT_SLOT = COUNT * 8 + 4; // int abort flag
 };
@@ -161,6 +162,7 @@ enum Site : int {
     SITE_PROD_KEMPTY = 0x101, SITE_PROD_VEMPTY = 0x102,
     SITE_MMA_Q = 0x201, SITE_MMA_K = 0x202, SITE_MMA_V = 0x203, SITE_MMA_P = 0x204,
     SITE_SM_S = 0x301, SITE_SM_O = 0x302, SITE_SM_Q = 0x303, SITE_SM_KS = 0x304, SITE_SM_EPI = 0x305,
+    SITE_SM_TOKEN = 0x306,
 };
 
 struct Work {
@@ -327,6 +329,14 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
     tile_blocks<T>(p, row0, w.valid[t], a, e);
     int klo, khi;
     row_keys(p, q, klo, khi);
+    // Exp-phase order between the two softmax warpgroups: WG0 k, WG1 k, WG0 k+1, ...
+    // (k = each tile's own iteration count), so the MUFU serves one warpgroup at a time.
+    int other_iters = 0;
+    if constexpr (T::NT == 2) {
+        int oa, oe;
+        tile_blocks<T>(p, w.row0[1 - t], w.valid[1 - t], oa, oe);
+        other_iters = oe - oa;
+    }
 
     const float sl2 = p.scale_log2;
     float m_ref = -INFINITY;
@@ -482,6 +492,14 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         // P = exp2(s*scale*log2e - m); the row sum uses the unrounded values
         const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
         float lsum = 0.f;
+        if constexpr (T::NT == 2) {
+            const int need = it - 1 + t;  // the other warpgroup's exp phase that comes first
+            if (need >= 0 && need < other_iters &&
+                !warp_wait(bar(Bars::EXPD + (1 - t)), need & 1, ab, SITE_SM_TOKEN)) {
+                aborted = true;
+                continue;
+            }
+        }
         // P goes back over S in 32-key chunks (S is already in registers), so only
         // one chunk of packed P is live at a time.  8 independent partial sums keep
         // the row-sum dependency chain short.
@@ -535,6 +553,10 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         }
         lsum = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         l += lsum;
+        if constexpr (T::NT == 2) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(Bars::EXPD + t));
+        }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -797,6 +819,7 @@ __global__ void __launch_bounds__(T::THREADS, 1)
             mbar_init(bar(Bars::KS_FULL + 2 * t), 128);
             mbar_init(bar(Bars::KS_FULL + 2 * t + 1), 128);
             mbar_init(bar(Bars::EPI + t), 128);
+            mbar_init(bar(Bars::EXPD + t), 4);
         }
         fence_barrier_init();
     }
