@@ -255,7 +255,9 @@ def time_e2e(cfg, x, steps, warmup, dist_on):
 # ---------------------------------------------------------------- CPU baseline
 def cpu_baseline(cfg, max_seconds=10.0):
     """The oracle port (fp32 torch on the host cores) on a bounded sample: whole query
-    heads of batch 0 of the same workload, until ~max_seconds of CPU work."""
+    heads of the same workload (the heads of one KV group, repeated for the next
+    groups: each head is the same amount of work), until ~max_seconds of CPU work or
+    the whole workload."""
     from oracle import torch_oracle
 
     g = torch.Generator().manual_seed(0)
@@ -272,20 +274,23 @@ def cpu_baseline(cfg, max_seconds=10.0):
     from oracle.torch_oracle import flops as _fl
 
     done_units, heads = 0.0, 0
+    total_heads = cfg["B"] * H
     t0 = time.perf_counter()
-    while heads < G and (time.perf_counter() - t0) < max_seconds:
+    while heads < total_heads and (heads == 0 or (time.perf_counter() - t0) < max_seconds):
+        h = heads % G
         torch_oracle.attention(q, k, v, causal=cfg["causal"], window=cfg["window"], rot_cos=cos, rot_sin=sin,
-                               heads=range(heads, heads + 1))
+                               heads=range(h, h + 1))
         heads += 1
     secs = time.perf_counter() - t0
     if cfg["kind"] == "decode":
-        done_units = 2 * KS * D * 2 + 2 * S * D * 2 * heads  # bytes of the sampled heads' K/V + q/o
+        groups = (heads + G - 1) // G  # each KV group streams its K/V once for its G heads
+        done_units = groups * 2 * KS * D * 2 + 2 * S * D * 2 * heads  # K/V + q/o bytes
         value = done_units / secs / 1e9
     else:
         done_units = _fl(1, heads, S, KS, D, cfg["causal"], cfg["window"])
         value = done_units / secs / 1e12
     return {"value": value, "unit": metric_of(cfg)[1], "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{heads} query head(s) of batch 0 / kv group 0, fp32 torch oracle, {secs:.2f} s",
+            "sample": f"{heads} query head(s) of {total_heads} (S={S}, KS={KS}, D={D}), fp32 torch oracle, {secs:.1f} s",
             "host_cpu_count": os.cpu_count()}
 
 

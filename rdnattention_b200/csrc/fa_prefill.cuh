@@ -16,21 +16,29 @@
 //   warp 4*NT         TMA producer (one lane): Q tiles once, then a ring of
 //                     K tiles and a ring of V tiles.
 //   warp 4*NT+1       MMA issuer (one lane): S_t = Q_t K^T (SS form),
-//                     O_t += P_t V (TS form, P read from TMEM).  Per block j
-//                     it issues, for each tile, PV(j) then QK(j+1), so one
-//                     tile's softmax overlaps the other tile's MMAs.
-//   warps 4*NT+2..+3  idle; they complete the control warpgroup so that the
-//                     NT = 2 kernel can move registers from it to the softmax
-//                     warpgroups (setmaxnreg: 200 / 80 per thread, launched
-//                     at 168).
+//                     O_t += P_t V (TS form, P read from TMEM).
+//   warp 4*NT+2       second MMA issuer when S is double-buffered (tile 1's
+//                     MMAs), else idle.
+//   warp 4*NT+3       idle; completes the control warpgroup so that the NT = 2
+//                     kernel can move registers between warpgroups (setmaxnreg).
+//
+// Two schedules:
+//   * single-buffered S (128-key blocks; INT8, head_dim > 128): per block j
+//     and tile, PV(j) then QK(j+1) into the same TMEM columns, so a tile's
+//     next S waits for its PV; the other tile's softmax fills the gap.
+//   * double-buffered S (FP16 head_dim <= 128, 64-key blocks): S(t, j) lives
+//     in buffer (j - first block) & 1; QK(j+2) is issued right after PV(j)
+//     into the buffer PV(j) just read, so a tile's softmax only ever waits
+//     for S itself.  An O rescale waits for PV(j-1) on its own barrier.
+//     With two tiles each tile has its own MMA issuer thread.
 //
 // RoPE is not applied here: rope.cuh rotates Q and K once per launch and the
 // kernel reads the rotated copies (rotating inside every CTA would repeat the
 // K rotation once per query tile that reads the block).
 //
-// TMEM columns: S_t at [t*BC, t*BC+BC) (P aliases its first columns);
-// FP16: O_t (fp32) after all S.  INT8: ACC_t (s32 PV accumulator) then
-// O_t (fp32, flushed from ACC whenever the row max moves).
+// TMEM columns: S(t, b) at [(t*NSB + b)*BC, +BC) (P aliases its first
+// columns); FP16: O_t (fp32) after all S.  INT8: ACC_t (s32 PV accumulator)
+// then O_t (fp32, flushed from ACC whenever the row max moves).
 //
 // Semantics follow the reference kernel (src/rdna/fa2_forward_f16.hip:633-741,
 // src/rdna/fa2_forward_int8qk.hip:229-495): exp2-domain online softmax with
@@ -50,6 +58,9 @@ namespace prefill {
 using namespace sm100;
 
 constexpr int BM = 128;  // query rows per tile (= TMEM lanes)
+#ifndef RDNA_EXP_TOKEN
+#define RDNA_EXP_TOKEN 1
+#endif
 
 struct Params {
     int B, H, Hkv, S, KS;
@@ -69,7 +80,7 @@ struct Params {
     const float* k_vec;
 };
 
-template <int D_, int DVMAX_, int BC_, int NT_, int NSK_, int NSV_, bool I8_>
+template <int D_, int DVMAX_, int BC_, int NT_, int NSK_, int NSV_, bool I8_, bool SDB_ = false>
 struct Traits {
     static constexpr int D = D_;          // QK depth (head_dim)
     static constexpr int DVMAX = DVMAX_;  // output columns per CTA (<= 256)
@@ -78,6 +89,20 @@ struct Traits {
     static constexpr int NSK = NSK_;
     static constexpr int NSV = NSV_;
     static constexpr bool I8 = I8_;
+    // S double-buffered in TMEM: QK(j+2) is issued right after PV(j), while
+    // the softmax works on S(j+1) from the other buffer.
+    static constexpr bool SDB = SDB_;
+    static constexpr int NSB = SDB ? 2 : 1;
+    // MMA issuer threads: with double-buffered S and two tiles, each tile has
+    // its own issuer (warps WARP_MMA and WARP_MMA + 1), so one tile's barrier
+    // waits overlap the other tile's MMA issue.  K/V ring slots are released
+    // once every issuer has committed.
+    static constexpr int NI = (SDB && NT == 2) ? 2 : 1;
+    // Exp-phase token between the two softmax warpgroups (one warpgroup on the
+    // MUFU at a time).
+    static constexpr bool TOKEN = NT == 2 && RDNA_EXP_TOKEN;
+    static_assert(!(SDB && I8), "S double buffering is FP16-only");
+    static_assert(NSK <= 8 && NSV <= 8 && (!SDB || NSV >= 2), "ring depth");
     static constexpr int ESZ = I8 ? 1 : 2;
     static constexpr int ROW_BYTES = D * ESZ;
     static constexpr int SW = (ROW_BYTES % 128 == 0) ? 128 : 64;  // swizzle span (bytes)
@@ -98,15 +123,18 @@ struct Traits {
     // Register split (NT = 2 only): launched at LAUNCH_REGS per thread.
     static constexpr bool RESPLIT = NT == 2;
     static constexpr int LAUNCH_REGS = 168;
-    static constexpr int SOFTMAX_REGS = 216;
-    static constexpr int CONTROL_REGS = 56;
+    // 128-key blocks hold 128 scores per softmax thread; 64-key blocks (S
+    // double-buffered) need far fewer, and the two MMA issuer warps then keep
+    // enough registers not to spill.
+    static constexpr int SOFTMAX_REGS = SDB ? 176 : 216;
+    static constexpr int CONTROL_REGS = SDB ? 152 : 56;
     static_assert(!RESPLIT || 256 * SOFTMAX_REGS + 128 * CONTROL_REGS <= THREADS * LAUNCH_REGS,
                   "register split exceeds the launch allocation");
 
     // TMEM columns
-    static constexpr int S_COL0 = 0;
-    static constexpr int ACC_COL0 = NT * BC;                         // INT8 only
-    static constexpr int O_COL0 = I8 ? NT * BC + NT * DVMAX : NT * BC;
+    static constexpr int S_COL0 = 0;                                 // S(t, b) at (t * NSB + b) * BC
+    static constexpr int ACC_COL0 = NT * NSB * BC;                   // INT8 only
+    static constexpr int O_COL0 = I8 ? NT * BC + NT * DVMAX : NT * NSB * BC;
     static constexpr int TMEM_USED = O_COL0 + NT * DVMAX;
     static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                      : TMEM_USED <= 256 ? 256 : 512;
@@ -143,16 +171,17 @@ struct Traits {
 struct Bars {
     static constexpr int Q_FULL = 0, DRAIN = 2;
     static constexpr int K_FULL = 4;      // +NSK
-    static constexpr int K_EMPTY = 20;    // +NSK
-    static constexpr int V_FULL = 28;     // +NSV
-    static constexpr int V_EMPTY = 36;    // +NSV
-    static constexpr int S_FULL = 44;     // +NT
-    static constexpr int P_FULL = 46;     // +NT
-    static constexpr int O_FULL = 48;     // +NT
-    static constexpr int KS_FULL = 50;    // +2*NT (INT8 per-key scale handoff, by block parity)
-    static constexpr int EPI = 54;        // +NT (O staging written)
-    static constexpr int EXPD = 56;       // +NT (softmax exp phase finished, one arrive per warp)
-    static constexpr int COUNT = 58;
+    static constexpr int K_EMPTY = 12;    // +NSK
+    static constexpr int V_FULL = 20;     // +NSV
+    static constexpr int V_EMPTY = 28;    // +NSV
+    static constexpr int S_FULL = 36;     // +t*NSB+b
+    static constexpr int P_FULL = 40;     // +t*NSB+b
+    static constexpr int O_FULL = 44;     // +NT
+    static constexpr int PV_DONE = 46;    // +NT (each PV(t, j) complete; SDB only)
+    static constexpr int KS_FULL = 48;    // +2*NT (INT8 per-key scale handoff, by block parity)
+    static constexpr int EPI = 52;        // +NT (O staging written)
+    static constexpr int EXPD = 54;       // +NT (softmax exp phase finished, one arrive per warp)
+    static constexpr int COUNT = 56;
     static constexpr int TMEM_SLOT = COUNT * 8;      // u32 TMEM base
     static constexpr int ABORT_SLOT = COUNT * 8 + 4; // int abort flag
 };
@@ -162,7 +191,7 @@ enum Site : int {
     SITE_PROD_KEMPTY = 0x101, SITE_PROD_VEMPTY = 0x102,
     SITE_MMA_Q = 0x201, SITE_MMA_K = 0x202, SITE_MMA_V = 0x203, SITE_MMA_P = 0x204,
     SITE_SM_S = 0x301, SITE_SM_O = 0x302, SITE_SM_Q = 0x303, SITE_SM_KS = 0x304, SITE_SM_EPI = 0x305,
-    SITE_SM_TOKEN = 0x306,
+    SITE_SM_TOKEN = 0x306, SITE_SM_PV = 0x307,
 };
 
 struct Work {
@@ -316,7 +345,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
     const int wq = warp % 4;
     const int r = wq * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t tS = tmem + lane_base + T::S_COL0 + t * T::BC;
+    const uint32_t tS0 = tmem + lane_base + T::S_COL0 + t * T::NSB * T::BC;
     const uint32_t tO = tmem + lane_base + T::O_COL0 + t * T::DVMAX;
     const uint32_t tACC = tmem + lane_base + T::ACC_COL0 + t * T::DVMAX;
     const uint32_t bars = smem_u32(smem);
@@ -332,7 +361,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
     // Exp-phase order between the two softmax warpgroups: WG0 k, WG1 k, WG0 k+1, ...
     // (k = each tile's own iteration count), so the MUFU serves one warpgroup at a time.
     int other_iters = 0;
-    if constexpr (T::NT == 2) {
+    if constexpr (T::TOKEN) {
         int oa, oe;
         tile_blocks<T>(p, w.row0[1 - t], w.valid[1 - t], oa, oe);
         other_iters = oe - oa;
@@ -379,7 +408,11 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
                     aborted = true;
             }
         }
-        if (!aborted && !warp_wait(bar(Bars::S_FULL + t), it & 1, ab, SITE_SM_S)) aborted = true;
+        // S buffer of this block, and the phase of its barrier
+        const int sb = T::SDB ? (it & 1) : 0;
+        const uint32_t tS = tS0 + sb * T::BC;
+        const uint32_t s_par = T::SDB ? ((it >> 1) & 1) : (it & 1);
+        if (!aborted && !warp_wait(bar(Bars::S_FULL + t * T::NSB + sb), s_par, ab, SITE_SM_S)) aborted = true;
         if (aborted) continue;
         tc_fence_after();
 
@@ -447,8 +480,18 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         }
 
         if constexpr (!T::I8) {
-            // O(tmem) *= corr.  PV(j-1) is complete: S_FULL(j) was committed after it.
+            // O(tmem) *= corr once PV(j-1) is complete.  Single-buffered S: S_FULL(j)
+            // was committed after PV(j-1).  Double-buffered: wait for PV_DONE phase
+            // it-1; PV(j) cannot have been issued yet (it needs this warp's P), so
+            // the barrier is at most one phase ahead and the parity is unambiguous.
             if (__any_sync(0xffffffffu, rescale)) {
+                if constexpr (T::SDB) {
+                    if (!warp_wait(bar(Bars::PV_DONE + t), (it - 1) & 1, ab, SITE_SM_PV)) {
+                        aborted = true;
+                        continue;
+                    }
+                    tc_fence_after();
+                }
                 const float c = rescale ? corr : 1.f;
                 for (int c0 = 0; c0 < dv; c0 += 32) {
                     uint32_t o[32];
@@ -492,7 +535,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         // P = exp2(s*scale*log2e - m); the row sum uses the unrounded values
         const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
         float lsum = 0.f;
-        if constexpr (T::NT == 2) {
+        if constexpr (T::TOKEN) {
             const int need = it - 1 + t;  // the other warpgroup's exp phase that comes first
             if (need >= 0 && need < other_iters &&
                 !warp_wait(bar(Bars::EXPD + (1 - t)), need & 1, ab, SITE_SM_TOKEN)) {
@@ -553,14 +596,14 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         }
         lsum = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         l += lsum;
-        if constexpr (T::NT == 2) {
+        if constexpr (T::TOKEN) {
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(Bars::EXPD + t));
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(Bars::P_FULL + t));
+        if (lane == 0) mbar_arrive(bar(Bars::P_FULL + t * T::NSB + sb));
     }
 
     // ---------------------------------------------------------------- epilogue
@@ -682,16 +725,33 @@ __device__ void producer_role(const Params& p, const CUtensorMap* tmQ, const CUt
 }
 
 // ------------------------------------------------------------------- MMA
+// Shared-memory descriptors of the MMA operands, built once per CTA: a tile's
+// descriptor is its base descriptor plus (byte offset >> 4) in the 14-bit
+// start-address field (shared addresses stay below 2^18 bytes, so the field
+// never carries), which keeps the MMA issuer at one add per operand.
 template <class T>
-__device__ __forceinline__ void issue_qk(uint8_t* smem, uint32_t tmem, int t, int kslot) {
-    const uint32_t qa = smem_u32(smem + T::OFF_Q + t * T::Q_TILE);
-    const uint32_t kb = smem_u32(smem + T::OFF_K + kslot * T::K_TILE);
-    const uint32_t d = tmem + T::S_COL0 + t * T::BC;
+struct Descs {
+    uint64_t q0;  // Q tile 0 (K-major)
+    uint64_t k0;  // K ring slot 0 (K-major)
+    uint64_t v0;  // V ring slot 0 (MN-major)
+    __device__ __forceinline__ explicit Descs(uint8_t* smem) {
+        q0 = smem_desc(smem_u32(smem + T::OFF_Q), 16, 8 * T::SW, T::LAYOUT);
+        k0 = smem_desc(smem_u32(smem + T::OFF_K), 16, 8 * T::SW, T::LAYOUT);
+        // MN-major V: 8-key atoms SBO = 8*SW apart, box (BOX columns) LBO = BC*SW apart
+        v0 = smem_desc(smem_u32(smem + T::OFF_V), T::BC * T::SW, 8 * T::SW, T::LAYOUT);
+    }
+};
+
+template <class T>
+__device__ __forceinline__ void issue_qk(const Descs<T>& dz, uint32_t tmem, int t, int kslot, int sb = 0) {
+    const uint64_t qa = dz.q0 + static_cast<uint32_t>(t * (T::Q_TILE >> 4));
+    const uint64_t kb = dz.k0 + static_cast<uint32_t>(kslot * (T::K_TILE >> 4));
+    const uint32_t d = tmem + T::S_COL0 + (t * T::NSB + sb) * T::BC;
 #pragma unroll
     for (int kk = 0; kk < T::D / T::KSTEP; ++kk) {
         const int box = kk / T::STEPS_PER_BOX, sub = kk % T::STEPS_PER_BOX;
-        const uint64_t ad = smem_desc(qa + box * T::Q_BOX_BYTES + sub * 32, 16, 8 * T::SW, T::LAYOUT);
-        const uint64_t bd = smem_desc(kb + box * T::K_BOX_BYTES + sub * 32, 16, 8 * T::SW, T::LAYOUT);
+        const uint64_t ad = qa + static_cast<uint32_t>((box * T::Q_BOX_BYTES + sub * 32) >> 4);
+        const uint64_t bd = kb + static_cast<uint32_t>((box * T::K_BOX_BYTES + sub * 32) >> 4);
         if constexpr (T::I8)
             mma_i8_ss(d, ad, bd, T::IDESC_QK, kk > 0 ? 1u : 0u);
         else
@@ -700,21 +760,100 @@ __device__ __forceinline__ void issue_qk(uint8_t* smem, uint32_t tmem, int t, in
 }
 
 template <class T>
-__device__ __forceinline__ void issue_pv(uint8_t* smem, uint32_t tmem, int t, int vslot, bool accumulate,
-                                         uint32_t idesc_pv) {
-    const uint32_t vb = smem_u32(smem + T::OFF_V + vslot * T::V_TILE);
-    const uint32_t a_base = tmem + T::S_COL0 + t * T::BC;  // P aliases S
+__device__ __forceinline__ void issue_pv(const Descs<T>& dz, uint32_t tmem, int t, int vslot, bool accumulate,
+                                         uint32_t idesc_pv, int sb = 0) {
+    const uint64_t vb = dz.v0 + static_cast<uint32_t>(vslot * (T::V_TILE >> 4));
+    const uint32_t a_base = tmem + T::S_COL0 + (t * T::NSB + sb) * T::BC;  // P aliases S
     const uint32_t d = tmem + (T::I8 ? T::ACC_COL0 : T::O_COL0) + t * T::DVMAX;
 #pragma unroll
     for (int kk = 0; kk < T::BC / T::KSTEP; ++kk) {
-        // MN-major V: 8-key atoms SBO = 8*SW apart, box (BOX columns) LBO = BC*SW apart
-        const uint64_t bd = smem_desc(vb + kk * T::KSTEP * T::SW, T::BC * T::SW, 8 * T::SW, T::LAYOUT);
+        const uint64_t bd = vb + static_cast<uint32_t>((kk * T::KSTEP * T::SW) >> 4);
         const uint32_t acc = (kk > 0 || accumulate) ? 1u : 0u;
         if constexpr (T::I8)
             mma_i8_ts(d, a_base + kk * 8, bd, idesc_pv, acc);
         else
             mma_f16_ts(d, a_base + kk * 8, bd, idesc_pv, acc);
     }
+}
+
+// Double-buffered S: S(t, j) lives in buffer (j - ta[t]) & 1.  The prologue
+// issues QK for the first two blocks; block j then issues, per tile, PV(j)
+// (after P(t, j) is published) and QK(j+2) into the buffer PV(j) just read
+// (tcgen05 MMAs from one thread run in issue order).  The softmax of block
+// j+1 meanwhile works on the other buffer, so a tile's softmax never waits
+// for the tensor core except for S itself.
+template <class T>
+__device__ void mma_role_sdb(const Params& p, const Work& w, int jlo, int jhi, const int* ta, const int* te,
+                             uint8_t* smem, uint32_t tmem, const Abort& ab, int dv, int issuer) {
+    // issuer i serves tiles [t_begin, t_end)
+    const int t_begin = T::NI == 1 ? 0 : issuer;
+    const int t_end = T::NI == 1 ? T::NT : issuer + 1;
+    const uint32_t bars = smem_u32(smem);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+    const uint32_t idesc_pv = instr_desc(1u, 0u, 1u, BM, static_cast<uint32_t>(dv));
+    const Descs<T> dz(smem);
+    bool ok = mbar_wait(bar(Bars::Q_FULL), 0, ab, SITE_MMA_Q);
+    tc_fence_after();
+    int kc = 0, vc = 0;
+    for (int jj = jlo; ok && jj < jhi && jj < jlo + 2; ++jj) {
+        const int ks = kc % T::NSK;
+        if (!mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+            ok = false;
+            break;
+        }
+        tc_fence_after();
+        for (int t = t_begin; t < t_end; ++t) {
+            if (ta[t] <= jj && jj < te[t]) {
+                const int sb = (jj - ta[t]) & 1;
+                issue_qk<T>(dz, tmem, t, ks, sb);
+                tc_commit(bar(Bars::S_FULL + t * T::NSB + sb));
+            }
+        }
+        tc_commit(bar(Bars::K_EMPTY + ks));
+        kc++;
+    }
+    for (int j = jlo; ok && j < jhi; ++j) {
+        const int vs = vc % T::NSV;
+        if (!mbar_wait(bar(Bars::V_FULL + vs), (vc / T::NSV) & 1, ab, SITE_MMA_V)) {
+            ok = false;
+            break;
+        }
+        const bool has_k = j + 2 < jhi;
+        const int ks = kc % T::NSK;
+        if (has_k && !mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+            ok = false;
+            break;
+        }
+        tc_fence_after();
+        for (int t = t_begin; t < t_end; ++t) {
+            if (ta[t] <= j && j < te[t]) {
+                const int it = j - ta[t];
+                const int sb = it & 1;
+                if (!mbar_wait(bar(Bars::P_FULL + t * T::NSB + sb), (it >> 1) & 1, ab, SITE_MMA_P)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                issue_pv<T>(dz, tmem, t, vs, it > 0, idesc_pv, sb);
+                tc_commit(bar(Bars::PV_DONE + t));
+                if (j == te[t] - 1) tc_commit(bar(Bars::O_FULL + t));
+            }
+            if (has_k && ta[t] <= j + 2 && j + 2 < te[t]) {
+                const int sb = (j + 2 - ta[t]) & 1;
+                issue_qk<T>(dz, tmem, t, ks, sb);
+                tc_commit(bar(Bars::S_FULL + t * T::NSB + sb));
+            }
+        }
+        if (!ok) break;
+        tc_commit(bar(Bars::V_EMPTY + vs));
+        vc++;
+        if (has_k) {
+            tc_commit(bar(Bars::K_EMPTY + ks));
+            kc++;
+        }
+    }
+    tc_commit(bar(Bars::DRAIN + issuer));
+    mbar_wait_drain(bar(Bars::DRAIN + issuer), 0);
 }
 
 template <class T>
@@ -724,6 +863,7 @@ __device__ void mma_role(const Params& p, const Work& w, int jlo, int jhi, const
     auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
     const int kready = Bars::K_FULL;
     const uint32_t idesc_pv = instr_desc(T::I8 ? 2u : 1u, T::I8 ? 1u : 0u, 1u, BM, static_cast<uint32_t>(dv));
+    const Descs<T> dz(smem);
     bool ok = mbar_wait(bar(Bars::Q_FULL), 0, ab, SITE_MMA_Q);
     tc_fence_after();
     int kc = 0, vc = 0;
@@ -734,7 +874,7 @@ __device__ void mma_role(const Params& p, const Work& w, int jlo, int jhi, const
             tc_fence_after();
             for (int t = 0; t < T::NT; ++t) {
                 if (ta[t] <= jlo && jlo < te[t]) {
-                    issue_qk<T>(smem, tmem, t, 0);
+                    issue_qk<T>(dz, tmem, t, 0);
                     tc_commit(bar(Bars::S_FULL + t));
                 }
             }
@@ -765,11 +905,11 @@ __device__ void mma_role(const Params& p, const Work& w, int jlo, int jhi, const
                 }
                 pc[t]++;
                 tc_fence_after();
-                issue_pv<T>(smem, tmem, t, vs, j > ta[t], idesc_pv);
+                issue_pv<T>(dz, tmem, t, vs, j > ta[t], idesc_pv);
                 if (j == te[t] - 1) tc_commit(bar(Bars::O_FULL + t));
             }
             if (act_next) {
-                issue_qk<T>(smem, tmem, t, ks);
+                issue_qk<T>(dz, tmem, t, ks);
                 tc_commit(bar(Bars::S_FULL + t));
             }
         }
@@ -804,18 +944,22 @@ __global__ void __launch_bounds__(T::THREADS, 1)
         *abort_flag = 0;
         mbar_init(bar(Bars::Q_FULL), 1);
         mbar_init(bar(Bars::DRAIN), 1);
+        mbar_init(bar(Bars::DRAIN + 1), 1);
         for (int s = 0; s < T::NSK; ++s) {
             mbar_init(bar(Bars::K_FULL + s), 1);
-            mbar_init(bar(Bars::K_EMPTY + s), 1);
+            mbar_init(bar(Bars::K_EMPTY + s), T::NI);
         }
         for (int s = 0; s < T::NSV; ++s) {
             mbar_init(bar(Bars::V_FULL + s), 1);
-            mbar_init(bar(Bars::V_EMPTY + s), 1);
+            mbar_init(bar(Bars::V_EMPTY + s), T::NI);
         }
         for (int t = 0; t < T::NT; ++t) {
-            mbar_init(bar(Bars::S_FULL + t), 1);
-            mbar_init(bar(Bars::P_FULL + t), 4);
+            for (int sb = 0; sb < T::NSB; ++sb) {
+                mbar_init(bar(Bars::S_FULL + t * T::NSB + sb), 1);
+                mbar_init(bar(Bars::P_FULL + t * T::NSB + sb), 4);
+            }
             mbar_init(bar(Bars::O_FULL + t), 1);
+            mbar_init(bar(Bars::PV_DONE + t), 1);
             mbar_init(bar(Bars::KS_FULL + 2 * t), 128);
             mbar_init(bar(Bars::KS_FULL + 2 * t + 1), 128);
             mbar_init(bar(Bars::EPI + t), 128);
@@ -865,7 +1009,17 @@ __global__ void __launch_bounds__(T::THREADS, 1)
         if (sm100::lane_id() == 0) producer_role<T>(p, &tmQ, &tmK, &tmV, w, jlo, jhi, smem, ab, dv, dv0);
         __syncwarp();
     } else if (warp == T::WARP_MMA) {
-        if (sm100::lane_id() == 0) mma_role<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv);
+        if (sm100::lane_id() == 0) {
+            if constexpr (T::SDB)
+                mma_role_sdb<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv, 0);
+            else
+                mma_role<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv);
+        }
+        __syncwarp();
+    } else if (T::NI == 2 && warp == T::WARP_MMA + 1) {
+        if constexpr (T::SDB) {
+            if (sm100::lane_id() == 0) mma_role_sdb<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv, 1);
+        }
         __syncwarp();
     }
     __syncthreads();

@@ -195,9 +195,10 @@ int dispatch_f16_dim(char* err, const Common& c, const prefill::Params& p, cudaS
     using namespace prefill;
     constexpr CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     if constexpr (D <= 128) {
-        // two 128-row tiles per CTA, 128-key blocks
-        constexpr int stages = D <= 32 ? 4 : D <= 64 ? 4 : D <= 96 ? 3 : 2;
-        return launch_prefill<Traits<D, D, 128, 2, stages, stages, false>>(err, c, p, st, dt);
+        // two 128-row tiles per CTA, 64-key blocks, S double-buffered in TMEM
+        // (2 tiles x 2 buffers x 64 columns + 2 x D columns of O <= 512)
+        constexpr int stages = D <= 64 ? 6 : D <= 96 ? 5 : 4;
+        return launch_prefill<Traits<D, D, 64, 2, stages, stages, false, true>>(err, c, p, st, dt);
     } else if constexpr (D <= 256) {
         // one tile per CTA (TMEM holds one O of up to 256 columns), 64-key blocks
         constexpr int stages = D <= 192 ? 3 : 2;

@@ -93,11 +93,29 @@ RDNA_DEV void record_error(const Abort& ab, int code) {
     atomicAdd(&g_rdna_status[1], 1);
 }
 
+// try_wait with an explicit suspend-time hint: a thread whose phase is not yet
+// complete is parked (woken when the phase completes, or after hint_ns) instead
+// of returning at once, so waiting warps do not take issue slots from the
+// warps that share their scheduler.
+RDNA_DEV bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 20000;  // 20 us per parked try_wait
+
 RDNA_DEV bool mbar_wait(uint32_t bar, uint32_t parity, const Abort& ab, int site) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) return true;
         if (*ab.flag) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
             record_error(ab, site);
