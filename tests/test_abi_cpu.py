@@ -142,3 +142,13 @@ def test_drop_in_import_name():
     assert rdnattention.flash_attn is R.flash_attn
     assert rdnattention.SUPPORTED_HEAD_DIMS == tuple(range(32, 513, 32))
     assert rdnattention.SUPPORTED_HEAD_DIMS_INT8 == (64, 128)
+
+
+def test_workspace_size_is_the_rotated_q_and_k():
+    """With RoPE the workspace holds the rotated Q and K written by the pre-pass:
+    B*H*S*D*2 and B*Hkv*KS*D*2 bytes, each rounded up to 256; none without RoPE."""
+    lib = R._lib_handle()
+    ws = lib.rdna_attention_forward_workspace_size
+    assert ws(4, 32, 8, 4096, 4096, 128, 1) == 4 * 32 * 4096 * 128 * 2 + 4 * 8 * 4096 * 128 * 2
+    assert ws(1, 3, 1, 5, 7, 32, 1) == 1024 + 512  # 960 and 448 bytes, each rounded up to a multiple of 256
+    assert ws(4, 32, 8, 4096, 4096, 128, 0) == 0
