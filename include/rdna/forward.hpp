@@ -58,6 +58,30 @@ struct ForwardParamsInt8QK {
     int32_t windowSize = -1;
     const void* qScaleVec = nullptr;  // const float*, (batch, heads, seq)
     const void* kScaleVec = nullptr;  // const float*, (batch, kv_heads, key_seq)
+    // Extension (no counterpart in the reference): const float*, (batch,
+    // kv_heads, head_dim); when set, output column d of every row is
+    // multiplied by it before the fp16 rounding (per-channel V dequantisation).
+    const void* vChannel = nullptr;
+};
+
+/// fp16 Q/K/V -> the operands of the INT8 path with per-token Q/K scales and a
+/// per-channel V scale (extension; no counterpart in the reference library,
+/// whose Python helpers do this on the host side with torch ops).
+struct QuantizeInt8Params {
+    const void* q = nullptr;  // fp16 [B, H, S, D], head_dim contiguous, strides in elements
+    const void* k = nullptr;  // fp16 [B, Hkv, KS, D]
+    const void* v = nullptr;  // fp16 [B, Hkv, KS, D]
+    int64_t qStrideB = 0, qStrideH = 0, qStrideS = 0;
+    int64_t kStrideB = 0, kStrideH = 0, kStrideS = 0;
+    int64_t vStrideB = 0, vStrideH = 0, vStrideS = 0;
+    uint32_t batchSize = 0, numHeads = 0, numKvHeads = 0, seqLen = 0, keySeqLen = 0;
+    uint32_t headDim = 0;     // 64 or 128
+    void* qInt8 = nullptr;    // int8 [B, H, S, D] contiguous
+    void* kInt8 = nullptr;    // int8 [B, Hkv, KS, D] contiguous
+    void* vInt8 = nullptr;    // int8 [B, Hkv, KS, D] contiguous
+    void* qScale = nullptr;   // float [B, H, S]
+    void* kScale = nullptr;   // float [B, Hkv, KS]
+    void* vChannel = nullptr; // float [B, Hkv, D]
 };
 
 /// Enqueues the FP16 forward on `stream` (a cudaStream_t). Non-blocking. 0 on success.
@@ -77,8 +101,10 @@ size_t noAllocWorkspaceLimit();
 const char* lastError();
 /// Enqueues the INT8 forward on `stream`. Non-blocking. 0 on success.
 int forwardInt8QK(const ForwardParamsInt8QK& params, void* stream);
-/// Reason the most recent forwardInt8QK() call on this thread failed, or nullptr.
+/// Reason the most recent forwardInt8QK() / quantizeInt8QKV() call on this thread failed, or nullptr.
 const char* lastErrorInt8QK();
+/// Enqueues the quantisation on `stream`. Non-blocking. 0 on success.
+int quantizeInt8QKV(const QuantizeInt8Params& params, void* stream);
 /// Whether a CUDA device is visible.
 bool hasDevice();
 

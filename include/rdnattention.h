@@ -141,6 +141,44 @@ RDNA_API int32_t rdna_attention_forward_noalloc(
     float scale, int32_t causal, int32_t has_rope, int32_t window_size,
     void* stream);
 
+/* rdna_attention_forward_int8qk plus a per-channel V scale: v_channel, when
+ * non-NULL, is fp32 (batch, num_kv_heads, head_dim) and multiplies output
+ * column d of every row before the single fp16 rounding (the reference
+ * applies the same factor afterwards, on the fp16 result, in its Python
+ * helper flash_attn_int8qk_quantized, rdnattention/__init__.py:346-357).
+ * Other arguments and return codes as rdna_attention_forward_int8qk. */
+RDNA_API int32_t rdna_attention_forward_int8qk_vch(
+    const void* q, const void* k, const void* v, void* output,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, float q_scale, float k_scale, float v_scale,
+    const void* q_scale_vec, const void* k_scale_vec, const void* v_channel,
+    int32_t causal, int32_t window_size, void* stream);
+
+/* fp16 Q/K/V (strided, element strides, head_dim contiguous) -> int8 operands
+ * for the INT8 path, on `stream`: q_scale (B, H, S) and k_scale (B, Hkv, KS)
+ * = per-row max|x| / 127 (0 -> 1), v_channel (B, Hkv, D) = per-column max
+ * over the key sequence of |v| / 127 (0 -> 1); int8 = round-half-even(x /
+ * scale) clamped to [-127, 127], written contiguous [B, H(kv), S, D].  Bit-
+ * identical to the reference's helpers quantize_int8_qk_pertoken (Q, K) and
+ * quantize_int8_perchannel_v (V) (rdnattention/__init__.py:303-343) run as
+ * torch ops on CUDA tensors (where max / 127 is a multiplication by the fp32
+ * reciprocal of 127).  head_dim 64 or 128.  Returns 0, or -3 with
+ * rdna_get_error() set ("Attention (int8qk) failed: ..."). */
+RDNA_API int32_t rdna_int8_quantize_qkv(
+    const void* q, const void* k, const void* v,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    void* q_int8, void* k_int8, void* v_int8,
+    void* q_scale, void* k_scale, void* v_channel, void* stream);
+
 /* Reads and clears the device status word of the current device: out[0] =
  * first error code a kernel recorded (a bounded wait that expired), out[1] =
  * number of such events.  Synchronises the current device.  Returns 0, or

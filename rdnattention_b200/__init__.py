@@ -69,6 +69,11 @@ def _lib_handle():
         lib.rdna_attention_forward_int8qk.argtypes = ([vp] * 4 + [i64] * 12 + [u32] * 6 + [f32] * 4 + [vp, vp]
                                                       + [i32, i32, vp])
         lib.rdna_attention_forward_int8qk.restype = i32
+        lib.rdna_attention_forward_int8qk_vch.argtypes = ([vp] * 4 + [i64] * 12 + [u32] * 6 + [f32] * 4
+                                                          + [vp, vp, vp] + [i32, i32, vp])
+        lib.rdna_attention_forward_int8qk_vch.restype = i32
+        lib.rdna_int8_quantize_qkv.argtypes = [vp] * 3 + [i64] * 9 + [u32] * 6 + [vp] * 7
+        lib.rdna_int8_quantize_qkv.restype = i32
         lib.rdna_debug_read_status.argtypes = [ctypes.POINTER(i32)]
         lib.rdna_debug_read_status.restype = i32
         _lib = lib
@@ -301,16 +306,77 @@ def quantize_int8_qk_pertoken(query, key):
     return qi, ki, q_scale, k_scale
 
 
+def quantize_int8_qkv(query, key, value):
+    """Device-side quantisation (one kernel) of fp16 Q/K/V for the INT8 path:
+    returns (qi, ki, vi, q_scale, k_scale, v_channel) — int8 contiguous
+    tensors, per-token float32 Q/K scales (batch, heads, seq) / (batch,
+    kv_heads, key_seq) and the per-channel V scale (batch, kv_heads,
+    head_dim).  Bit-identical to quantize_int8_qk_pertoken (qi, ki, scales)
+    and quantize_int8_perchannel_v (vi, v_channel).  head_dim 64 or 128;
+    query/key/value may be strided (head_dim contiguous).  Extension: the
+    reference does this with torch ops on the host side.
+    """
+    import torch
+
+    _validate_inputs(query, key, value, torch.float16, require_contiguous=False)
+    batch, heads, seq_len, head_dim = query.shape
+    _, kv_heads, key_seq_len, _ = key.shape
+    _check_head_dim(head_dim, "quantize_int8_qkv", allowed=SUPPORTED_HEAD_DIMS_INT8)
+    dev = query.device
+    qi = torch.empty(query.shape, dtype=torch.int8, device=dev)
+    ki = torch.empty(key.shape, dtype=torch.int8, device=dev)
+    vi = torch.empty(value.shape, dtype=torch.int8, device=dev)
+    q_scale = torch.empty(batch, heads, seq_len, dtype=torch.float32, device=dev)
+    k_scale = torch.empty(batch, kv_heads, key_seq_len, dtype=torch.float32, device=dev)
+    v_channel = torch.empty(batch, kv_heads, head_dim, dtype=torch.float32, device=dev)
+    qs, ks, vs = query.stride(), key.stride(), value.stride()
+    rc = _lib_handle().rdna_int8_quantize_qkv(
+        query.data_ptr(), key.data_ptr(), value.data_ptr(), qs[0], qs[1], qs[2], ks[0], ks[1], ks[2],
+        vs[0], vs[1], vs[2], batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+        qi.data_ptr(), ki.data_ptr(), vi.data_ptr(), q_scale.data_ptr(), k_scale.data_ptr(), v_channel.data_ptr(),
+        _stream_handle(dev))
+    if rc != 0:
+        raise RDNAttentionError(f"quantize_int8_qkv failed: {_last_error()}")
+    return qi, ki, vi, q_scale, k_scale, v_channel
+
+
 def flash_attn_int8qk_quantized(query, key, value, is_causal: bool = False, window_size: int = -1):
     """INT8 attention from fp16/fp32 Q/K/V — the recommended INT8 entry point:
     per-token Q/K scales in-kernel and an exact per-channel V rescale of the
     output.  Same contract as rdnattention/__init__.py:346-357.
+
+    fp16 inputs with head_dim 64/128 take the device path: one quantisation
+    kernel, then the INT8 kernel with the per-channel V scale applied in its
+    epilogue before the single fp16 rounding (the reference rescales the
+    fp16 output afterwards, a second rounding).  Other dtypes quantise with
+    the torch helpers first (exactly the reference's scales).
     """
-    _, _, vi, _, _, v_scale, v_channel = quantize_int8_perchannel_v(query, key, value)
-    qi, ki, q_scale, k_scale = quantize_int8_qk_pertoken(query, key)
-    out = flash_attn_int8qk(qi.contiguous(), ki.contiguous(), vi.contiguous(), q_scale, k_scale, v_scale,
-                            is_causal, window_size)
-    return (out.float() * v_channel.unsqueeze(-2)).to(out.dtype)
+    import torch
+
+    if (isinstance(query, torch.Tensor) and query.dtype == torch.float16 and query.is_cuda
+            and query.dim() == 4 and query.shape[-1] in SUPPORTED_HEAD_DIMS_INT8):
+        qi, ki, vi, q_scale, k_scale, v_channel = quantize_int8_qkv(query, key, value)
+        v_scale = 1.0
+    else:
+        _, _, vi, _, _, v_scale, v_channel = quantize_int8_perchannel_v(query, key, value)
+        qi, ki, q_scale, k_scale = quantize_int8_qk_pertoken(query, key)
+        qi, ki, vi = qi.contiguous(), ki.contiguous(), vi.contiguous()
+        v_channel = v_channel.contiguous()
+    _validate_inputs(qi, ki, vi, torch.int8)
+    batch, heads, seq_len, head_dim = qi.shape
+    _, kv_heads, key_seq_len, _ = ki.shape
+    _check_head_dim(head_dim, "flash_attn_int8qk", allowed=SUPPORTED_HEAD_DIMS_INT8)
+    out = torch.empty(qi.shape, dtype=torch.float16, device=qi.device)
+    qs, ks, vs, os_ = qi.stride(), ki.stride(), vi.stride(), out.stride()
+    rc = _lib_handle().rdna_attention_forward_int8qk_vch(
+        qi.data_ptr(), ki.data_ptr(), vi.data_ptr(), out.data_ptr(),
+        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
+        batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+        float(head_dim ** -0.5), 1.0, 1.0, float(v_scale), q_scale.data_ptr(), k_scale.data_ptr(),
+        v_channel.data_ptr(), 1 if is_causal else 0, int(window_size), _stream_handle(qi.device))
+    if rc != 0:
+        raise RDNAttentionError(f"flash_attn_int8qk failed: {_last_error()}")
+    return out
 
 
 def debug_read_status():
@@ -323,5 +389,5 @@ def debug_read_status():
 
 
 __all__ = ["flash_attn", "flash_attn_int8qk", "flash_attn_int8qk_quantized", "quantize_int8_perchannel_v",
-           "quantize_int8_qk_pertoken", "has_device", "RDNAttentionError", "SUPPORTED_HEAD_DIMS",
+           "quantize_int8_qk_pertoken", "quantize_int8_qkv", "has_device", "RDNAttentionError", "SUPPORTED_HEAD_DIMS",
            "SUPPORTED_HEAD_DIMS_INT8", "__version__"]

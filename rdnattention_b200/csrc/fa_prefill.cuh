@@ -13,14 +13,19 @@
 //                     keeps the running max / row sum, writes P (fp16 or
 //                     int8) back over S in TMEM, rescales O in TMEM when
 //                     needed, and runs the epilogue (O / l -> fp16 -> TMA store).
-//   warp 4*NT         TMA producer (one lane): Q tiles once, then a ring of
-//                     K tiles and a ring of V tiles.
+//   warp 4*NT         TMA producer (one lane): a ring of K tiles and a ring
+//                     of V tiles, across all of the CTA's work items.
 //   warp 4*NT+1       MMA issuer (one lane): S_t = Q_t K^T (SS form),
 //                     O_t += P_t V (TS form, P read from TMEM).
 //   warp 4*NT+2       second MMA issuer when S is double-buffered (tile 1's
 //                     MMAs), else idle.
-//   warp 4*NT+3       idle; completes the control warpgroup so that the NT = 2
-//                     kernel can move registers between warpgroups (setmaxnreg).
+//   warp 4*NT+3       Q producer (one lane): each item's Q tiles, once the
+//                     previous item's Q K^T MMAs no longer read the buffer.
+//
+// Persistent CTAs (the double-buffered kernels): one CTA per SM loops over
+// work items i, i + gridDim.x, ... (longest first); barrier phases run on
+// across items, so the next item's Q / K / V loads and first Q K^T overlap the
+// current item's last blocks and epilogue.  Other kernels run one item per CTA.
 //
 // Two schedules:
 //   * single-buffered S (128-key blocks; INT8, head_dim > 128): per block j
@@ -72,12 +77,14 @@ struct Params {
     int n_rb;     // ceil(S / BM)
     int n_rp;     // ceil(n_rb / 2)
     int n_split;  // output column slices per tile (head_dim > 256)
+    int n_items;  // work items (CTA i handles items i, i + gridDim.x, ...)
     int dv_split; // output columns per slice (multiple of the box width)
     float scale_log2;
     // INT8 path
     float q_scale, k_scale, pv_scale;
     const float* q_vec;
     const float* k_vec;
+    const float* v_chan;  // per-channel V scale (B, Hkv, D), or null
 };
 
 template <int D_, int DVMAX_, int BC_, int NT_, int NSK_, int NSV_, bool I8_, bool SDB_ = false>
@@ -98,9 +105,18 @@ struct Traits {
     // waits overlap the other tile's MMA issue.  K/V ring slots are released
     // once every issuer has committed.
     static constexpr int NI = (SDB && NT == 2) ? 2 : 1;
+    // Persistent CTAs (one per SM, looping over work items) for the
+    // double-buffered kernels: the next item's Q load and first MMAs overlap
+    // the current item's epilogue, and TMEM / barrier setup happens once.
+    // Off by default: with a static item split it measured 2-8 % slower than
+    // one CTA per item, whose order the hardware block scheduler balances.
+#ifndef RDNA_PERSIST
+#define RDNA_PERSIST 0
+#endif
+    static constexpr bool PERSIST = SDB && RDNA_PERSIST;
     // Exp-phase token between the two softmax warpgroups (one warpgroup on the
     // MUFU at a time).
-    static constexpr bool TOKEN = NT == 2 && RDNA_EXP_TOKEN;
+    static constexpr bool TOKEN = NT == 2 && !PERSIST && RDNA_EXP_TOKEN;
     static_assert(!(SDB && I8), "S double buffering is FP16-only");
     static_assert(NSK <= 8 && NSV <= 8 && (!SDB || NSV >= 2), "ring depth");
     static constexpr int ESZ = I8 ? 1 : 2;
@@ -120,6 +136,7 @@ struct Traits {
     static constexpr int THREADS = 128 * NT + 128;
     static constexpr int WARP_PROD = 4 * NT;
     static constexpr int WARP_MMA = 4 * NT + 1;
+    static constexpr int WARP_QLOAD = 4 * NT + 3;
     // Register split (NT = 2 only): launched at LAUNCH_REGS per thread.
     static constexpr bool RESPLIT = NT == 2;
     static constexpr int LAUNCH_REGS = 168;
@@ -142,9 +159,11 @@ struct Traits {
     static_assert(D % BOX == 0 && DVMAX % BOX == 0, "head_dim must tile into boxes");
     static_assert(BC % KSTEP == 0 && BC % 32 == 0, "key block");
 
-    // Output (fp16) staging geometry.  FP16: O uses Q's swizzle and box and is
-    // staged in Q_t's buffer.  INT8: fp16 rows are twice as wide as the int8
-    // Q rows, so O gets its own 128B-swizzled staging region.
+    // Output (fp16) staging geometry.  FP16: O uses Q's swizzle and box; it is
+    // staged in Q_t's buffer (one item per CTA) or in its own region
+    // (persistent CTAs, where the next item's Q lands during the epilogue).
+    // INT8: fp16 rows are twice as wide as the int8 Q rows, so O gets its own
+    // 128B-swizzled staging region.
     static constexpr int O_SW = I8 ? 128 : SW;
     static constexpr int O_BOX = O_SW / 2;
     static constexpr int O_BOX_BYTES = BM * O_SW;
@@ -157,11 +176,12 @@ struct Traits {
     static constexpr int OFF_Q = ((MISC_BYTES + 1023) / 1024) * 1024;
     static constexpr int OFF_K = OFF_Q + NT * Q_TILE;
     static constexpr int OFF_V = OFF_K + NSK * K_TILE;
-    static constexpr int OFF_O = I8 ? OFF_V + NSV * V_TILE : OFF_Q;
-    static constexpr int O_STRIDE = I8 ? O_TILE : Q_TILE;  // staging bytes between tiles
-    static constexpr int SMEM_BYTES = OFF_V + NSV * V_TILE + (I8 ? NT * O_TILE : 0) + 1024;  // + align slack
+    static constexpr bool OWN_STAGE = I8 || PERSIST;
+    static constexpr int OFF_O = OWN_STAGE ? OFF_V + NSV * V_TILE : OFF_Q;
+    static constexpr int O_STRIDE = OWN_STAGE ? O_TILE : Q_TILE;  // staging bytes between tiles
+    static constexpr int SMEM_BYTES = OFF_V + NSV * V_TILE + (OWN_STAGE ? NT * O_TILE : 0) + 1024;  // + align slack
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-    static_assert(I8 || O_TILE <= Q_TILE, "O staging fits in the Q tile");
+    static_assert(OWN_STAGE || O_TILE <= Q_TILE, "O staging fits in the Q tile");
 
     static constexpr uint32_t IDESC_QK = instr_desc(I8 ? 2u : 1u, I8 ? 1u : 0u, 0u, BM, BC);
     static constexpr float THRESH = I8 ? 0.0f : 8.0f;  // log2-domain slack before O is rescaled
@@ -181,7 +201,10 @@ struct Bars {
     static constexpr int KS_FULL = 48;    // +2*NT (INT8 per-key scale handoff, by block parity)
     static constexpr int EPI = 52;        // +NT (O staging written)
     static constexpr int EXPD = 54;       // +NT (softmax exp phase finished, one arrive per warp)
-    static constexpr int COUNT = 56;
+    static constexpr int Q_EMPTY = 56;    // Q tiles no longer read (every issuer commits once per item)
+    static constexpr int O_EMPTY = 57;    // +NT (O read out of TMEM by the epilogue, one arrive per warp)
+    static constexpr int STG_FREE = 59;   // +NT (O store has read the staging buffer)
+    static constexpr int COUNT = 61;
     static constexpr int TMEM_SLOT = COUNT * 8;      // u32 TMEM base
     static constexpr int ABORT_SLOT = COUNT * 8 + 4; // int abort flag
 };
@@ -191,7 +214,8 @@ enum Site : int {
     SITE_PROD_KEMPTY = 0x101, SITE_PROD_VEMPTY = 0x102,
     SITE_MMA_Q = 0x201, SITE_MMA_K = 0x202, SITE_MMA_V = 0x203, SITE_MMA_P = 0x204,
     SITE_SM_S = 0x301, SITE_SM_O = 0x302, SITE_SM_Q = 0x303, SITE_SM_KS = 0x304, SITE_SM_EPI = 0x305,
-    SITE_SM_TOKEN = 0x306, SITE_SM_PV = 0x307,
+    SITE_SM_TOKEN = 0x306, SITE_SM_PV = 0x307, SITE_SM_STG = 0x308,
+    SITE_PROD_QEMPTY = 0x103, SITE_MMA_OEMPTY = 0x205,
 };
 
 struct Work {
@@ -280,6 +304,50 @@ __device__ __forceinline__ void tile_blocks(const Params& p, int row0, bool vali
     e = hi / T::BC + 1;
 }
 
+// The r-th work item of this CTA, or -1 past the end.  Items are numbered
+// longest first; rounds alternate direction (CTA c takes item c in even
+// rounds and gridDim.x-1-c in odd ones), so a static split of causal work
+// stays balanced.  With one CTA per item (gridDim.x == n_items) round 0 is
+// the CTA's own item.
+__device__ __forceinline__ int item_at(const Params& p, int r) {
+    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+    const int64_t item = static_cast<int64_t>(r) * G + ((r & 1) ? G - 1 - c : c);
+    return item < p.n_items ? static_cast<int>(item) : -1;
+}
+
+// Everything a role needs to know about one work item.
+struct Item {
+    Work w;
+    int ta[2], te[2];  // per-tile key-block ranges [ta, te)
+    int jlo, jhi;      // union of the tiles' ranges (the blocks the producer loads)
+    int dv, dv0;       // output columns of this CTA: [dv0, dv0 + dv)
+};
+
+template <class T>
+__device__ __forceinline__ Item make_item(const Params& p, int item) {
+    Item I;
+    I.w = decode_work<T>(p, item);
+    if (p.n_split > 1) {
+        I.dv0 = I.w.split * p.dv_split;
+        I.dv = min(p.dv_split, T::D - I.dv0);
+    } else {
+        I.dv0 = 0;
+        I.dv = T::D < T::DVMAX ? T::D : T::DVMAX;
+    }
+    I.ta[0] = I.te[0] = I.ta[1] = I.te[1] = 0;
+    for (int t = 0; t < T::NT; ++t) tile_blocks<T>(p, I.w.row0[t], I.w.valid[t], I.ta[t], I.te[t]);
+    I.jlo = 1 << 30;
+    I.jhi = -1;
+    for (int t = 0; t < T::NT; ++t) {
+        if (I.te[t] > I.ta[t]) {
+            I.jlo = min(I.jlo, I.ta[t]);
+            I.jhi = max(I.jhi, I.te[t]);
+        }
+    }
+    if (I.jhi < 0) I.jlo = I.jhi = 0;
+    return I;
+}
+
 // Whether block j needs no per-element mask for any row of the tile.
 template <class T>
 __device__ __forceinline__ bool block_full(const Params& p, int row0, int j) {
@@ -338,8 +406,8 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const A
 // once and the work is skipped, so all threads reach the kernel's final
 // __syncthreads.
 template <class T>
-__device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work& w, int t, uint8_t* smem,
-                             uint32_t tmem, const Abort& ab, int dv, int dv0) {
+__device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uint8_t* smem, uint32_t tmem,
+                             const Abort& ab) {
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int wq = warp % 4;
@@ -350,27 +418,32 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
     const uint32_t tACC = tmem + lane_base + T::ACC_COL0 + t * T::DVMAX;
     const uint32_t bars = smem_u32(smem);
     auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+    const float sl2 = p.scale_log2;
+    bool aborted = false;
+    // phase counters carried across this CTA's items
+    int g = 0;     // key blocks of tile t done in earlier items (S / P / PV_DONE / KS phases)
+    int n_o = 0;   // earlier items in which tile t accumulated O (O_FULL / O_EMPTY phases)
+    int n_st = 0;  // earlier O stores of tile t (EPI / STG_FREE phases)
 
-    if (!w.valid[t]) return;  // uniform for the warpgroup
+    // non-persistent kernels: exactly one item (a trip count the compiler can see)
+    for (int n_it = 0; T::PERSIST || n_it < 1; ++n_it) {
+    const int item = item_at(p, n_it);
+    if (item < 0) break;
+    const Item I = make_item<T>(p, item);
+    const Work& w = I.w;
+    const int dv = I.dv, dv0 = I.dv0;
+    if (!w.valid[t]) continue;  // uniform for the warpgroup (no O store, no phases used)
     const int row0 = w.row0[t];
     const int q = row0 + r;
-    int a, e;
-    tile_blocks<T>(p, row0, w.valid[t], a, e);
+    const int a = I.ta[t], e = I.te[t];
     int klo, khi;
     row_keys(p, q, klo, khi);
     // Exp-phase order between the two softmax warpgroups: WG0 k, WG1 k, WG0 k+1, ...
     // (k = each tile's own iteration count), so the MUFU serves one warpgroup at a time.
-    int other_iters = 0;
-    if constexpr (T::TOKEN) {
-        int oa, oe;
-        tile_blocks<T>(p, w.row0[1 - t], w.valid[1 - t], oa, oe);
-        other_iters = oe - oa;
-    }
+    const int other_iters = T::TOKEN ? I.te[1 - t] - I.ta[1 - t] : 0;
 
-    const float sl2 = p.scale_log2;
     float m_ref = -INFINITY;
     float l = 0.f;
-    bool aborted = false;
 
     // INT8 state
     float rowscale = 1.f;
@@ -397,21 +470,22 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
 
     int it = 0;
     for (int j = a; j < e; ++j, ++it) {
+        const int gg = g + it;  // this block's index among all blocks of tile t in this CTA
         if constexpr (T::I8) {
             if (kvec) {
-                // stage this block's per-key scales; buffer (it & 1) is reused every second block
-                const int buf = it & 1;
+                // stage this block's per-key scales; buffer (gg & 1) is reused every second block
+                const int buf = gg & 1;
                 if (r < T::BC) ksbuf[buf * T::BC + r] = ks_next;
                 mbar_arrive(bar(Bars::KS_FULL + 2 * t + buf));
                 ks_next = load_ks(j + 1);
-                if (!aborted && !warp_wait(bar(Bars::KS_FULL + 2 * t + buf), (it >> 1) & 1, ab, SITE_SM_KS))
+                if (!aborted && !warp_wait(bar(Bars::KS_FULL + 2 * t + buf), (gg >> 1) & 1, ab, SITE_SM_KS))
                     aborted = true;
             }
         }
         // S buffer of this block, and the phase of its barrier
-        const int sb = T::SDB ? (it & 1) : 0;
+        const int sb = T::SDB ? (gg & 1) : 0;
         const uint32_t tS = tS0 + sb * T::BC;
-        const uint32_t s_par = T::SDB ? ((it >> 1) & 1) : (it & 1);
+        const uint32_t s_par = T::SDB ? ((gg >> 1) & 1) : (gg & 1);
         if (!aborted && !warp_wait(bar(Bars::S_FULL + t * T::NSB + sb), s_par, ab, SITE_SM_S)) aborted = true;
         if (aborted) continue;
         tc_fence_after();
@@ -427,7 +501,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
             // s32 -> float on the ALU (exact: |q.k| <= 127*127*D < 2^22).  x holds
             // float(acc) * k_scale; the per-row q_scale * scale * log2(e) (rowscale) is
             // applied to the max and folded into the exponent's FMA below.
-            const float* ksb = ksbuf + (it & 1) * T::BC;
+            const float* ksb = ksbuf + (gg & 1) * T::BC;
             if (kvec) {
 #pragma unroll
                 for (int c = 0; c < T::BC; ++c) x[c] = (i2f_biased(raw[c]) - 12582912.0f) * ksb[c];
@@ -482,11 +556,11 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         if constexpr (!T::I8) {
             // O(tmem) *= corr once PV(j-1) is complete.  Single-buffered S: S_FULL(j)
             // was committed after PV(j-1).  Double-buffered: wait for PV_DONE phase
-            // it-1; PV(j) cannot have been issued yet (it needs this warp's P), so
+            // gg-1; PV(j) cannot have been issued yet (it needs this warp's P), so
             // the barrier is at most one phase ahead and the parity is unambiguous.
             if (__any_sync(0xffffffffu, rescale)) {
                 if constexpr (T::SDB) {
-                    if (!warp_wait(bar(Bars::PV_DONE + t), (it - 1) & 1, ab, SITE_SM_PV)) {
+                    if (!warp_wait(bar(Bars::PV_DONE + t), (gg - 1) & 1, ab, SITE_SM_PV)) {
                         aborted = true;
                         continue;
                     }
@@ -608,10 +682,20 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
 
     // ---------------------------------------------------------------- epilogue
     const bool has_blocks = e > a;
-    if (!aborted && has_blocks && !warp_wait(bar(Bars::O_FULL + t), 0, ab, SITE_SM_O)) aborted = true;
+    if (!aborted && has_blocks && !warp_wait(bar(Bars::O_FULL + t), n_o & 1, ab, SITE_SM_O)) aborted = true;
     if (!aborted) tc_fence_after();
-    // FP16 stages O in Q_t's buffer: its TMA load must have landed
-    if (!aborted && !T::I8 && !warp_wait(bar(Bars::Q_FULL), 0, ab, SITE_SM_Q)) aborted = true;
+    if constexpr (!T::OWN_STAGE) {
+        // FP16 with one item per CTA stages O in Q_t's buffer: its TMA load must have landed
+        if (!aborted && !warp_wait(bar(Bars::Q_FULL), 0, ab, SITE_SM_Q)) aborted = true;
+    } else if (n_st > 0) {
+        // the previous item's store must have finished reading the staging buffer
+        // (issued an item ago, so the wait is normally already satisfied)
+        if (r == 0) {
+            bulk_wait_read_all();
+            mbar_arrive(bar(Bars::STG_FREE + t));
+        }
+        if (!aborted && !warp_wait(bar(Bars::STG_FREE + t), (n_st - 1) & 1, ab, SITE_SM_STG)) aborted = true;
+    }
 
     uint8_t* stage = smem + T::OFF_O + t * T::O_STRIDE;
     if (!aborted) {
@@ -629,6 +713,12 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
                         const float of = oflushed ? __uint_as_float(ov[i]) : 0.f;
                         o[i] = (of + static_cast<float>(static_cast<int>(acc[i])) * p.pv_scale) * inv;
                     }
+                    if (p.v_chan != nullptr) {
+                        // per-channel V dequantisation, folded in before the one fp16 rounding
+                        const float* vc = p.v_chan + (static_cast<int64_t>(w.b) * p.Hkv + w.kvh) * T::D + dv0 + c0;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= __ldg(vc + i);
+                    }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(ov[i]) * inv;
@@ -639,13 +729,13 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
             }
             // 32 fp16 = 4 chunks of 16 bytes
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
+            for (int g4 = 0; g4 < 4; ++g4) {
                 uint4 v;
-                v.x = pack_half2(o[8 * g + 0], o[8 * g + 1]);
-                v.y = pack_half2(o[8 * g + 2], o[8 * g + 3]);
-                v.z = pack_half2(o[8 * g + 4], o[8 * g + 5]);
-                v.w = pack_half2(o[8 * g + 6], o[8 * g + 7]);
-                const int col = c0 + 8 * g;
+                v.x = pack_half2(o[8 * g4 + 0], o[8 * g4 + 1]);
+                v.y = pack_half2(o[8 * g4 + 2], o[8 * g4 + 3]);
+                v.z = pack_half2(o[8 * g4 + 4], o[8 * g4 + 5]);
+                v.w = pack_half2(o[8 * g4 + 6], o[8 * g4 + 7]);
+                const int col = c0 + 8 * g4;
                 const int box = col / T::O_BOX;
                 const int chunk = (col % T::O_BOX) / 8;
                 *reinterpret_cast<uint4*>(stage + box * T::O_BOX_BYTES + swz_off<T::O_SW>(r, chunk)) = v;
@@ -653,70 +743,110 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, const Work
         }
         fence_proxy_async_smem();
     }
+    if (has_blocks) {
+        // O (and the INT8 accumulator) are out of TMEM: the next item's first PV may overwrite them
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(Bars::O_EMPTY + t));
+    }
     mbar_arrive(bar(Bars::EPI + t));
     if (r == 0) {
-        if (!aborted && mbar_wait(bar(Bars::EPI + t), 0, ab, SITE_SM_EPI) && !*ab.flag) {
+        if (!aborted && mbar_wait(bar(Bars::EPI + t), n_st & 1, ab, SITE_SM_EPI) && !*ab.flag) {
             const int nbox = dv / T::O_BOX;
             for (int bx = 0; bx < nbox; ++bx)
                 tma_store_4d(tmO, smem_u32(stage + bx * T::O_BOX_BYTES), dv0 + bx * T::O_BOX, row0, w.head[t], w.b);
             bulk_commit();
-            bulk_wait_read_all();
+            // one item per CTA: staging in Q's buffer, wait here; persistent:
+            // the next epilogue (or the exit below) waits
+            if constexpr (!T::OWN_STAGE) bulk_wait_read_all();
         }
+    }
+    g += e - a;
+    n_o += has_blocks ? 1 : 0;
+    ++n_st;
+    }  // items
+    if constexpr (T::OWN_STAGE) {
+        if (r == 0) bulk_wait_all();  // the last store has landed before the CTA exits
     }
 }
 
-// -------------------------------------------------------------- producer
+// ------------------------------------------------------------- producers
+// Two TMA producer lanes.  The K/V producer streams every item's K and V
+// blocks through the rings, whose slot and phase counters run on across
+// items, so the next item's first blocks load during the current item's tail.
+// The Q producer loads an item's Q tiles once the previous item's Q K^T MMAs
+// are done with the buffer (Q_EMPTY).
 template <class T>
-__device__ void producer_role(const Params& p, const CUtensorMap* tmQ, const CUtensorMap* tmK,
-                              const CUtensorMap* tmV, const Work& w, int jlo, int jhi, uint8_t* smem,
-                              const Abort& ab, int dv, int dv0) {
+__device__ void producer_q_role(const Params& p, const CUtensorMap* tmQ, uint8_t* smem, const Abort& ab) {
     const uint32_t bars = smem_u32(smem);
     auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
     prefetch_tmap(tmQ);
+    const uint64_t pol_q = policy_evict_first();
+    int qfill = 0;
+    for (int r = 0; T::PERSIST || r < 1; ++r) {
+        const int item = item_at(p, r);
+        if (item < 0) break;
+        const Work w = decode_work<T>(p, item);
+        if (qfill > 0 && !mbar_wait(bar(Bars::Q_EMPTY), (qfill - 1) & 1, ab, SITE_PROD_QEMPTY)) break;
+        mbar_arrive_expect_tx(bar(Bars::Q_FULL), T::NT * T::Q_TILE);
+        for (int t = 0; t < T::NT; ++t) {
+            const uint32_t dst = smem_u32(smem + T::OFF_Q + t * T::Q_TILE);
+            for (int bx = 0; bx < T::NBOX; ++bx)
+                tma_load_4d(dst + bx * T::Q_BOX_BYTES, tmQ, bar(Bars::Q_FULL), bx * T::BOX, w.row0[t], w.head[t],
+                            w.b, pol_q);
+        }
+        ++qfill;
+    }
+    // every issued copy lands before the CTA can exit
+    if (qfill > 0) mbar_wait_drain(bar(Bars::Q_FULL), (qfill - 1) & 1);
+}
+
+template <class T>
+__device__ void producer_kv_role(const Params& p, const CUtensorMap* tmK, const CUtensorMap* tmV, uint8_t* smem,
+                                 const Abort& ab) {
+    const uint32_t bars = smem_u32(smem);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
     prefetch_tmap(tmK);
     prefetch_tmap(tmV);
-    const uint64_t pol_q = policy_evict_first();
     const uint64_t pol_kv = policy_evict_last();
 
-    mbar_arrive_expect_tx(bar(Bars::Q_FULL), T::NT * T::Q_TILE);
-    for (int t = 0; t < T::NT; ++t) {
-        const uint32_t dst = smem_u32(smem + T::OFF_Q + t * T::Q_TILE);
-        for (int bx = 0; bx < T::NBOX; ++bx)
-            tma_load_4d(dst + bx * T::Q_BOX_BYTES, tmQ, bar(Bars::Q_FULL), bx * T::BOX, w.row0[t], w.head[t], w.b,
-                        pol_q);
-    }
-    const int nbox_v = dv / T::BOX;
     int kfill[T::NSK] = {0};
     int vfill[T::NSV] = {0};
     bool ok = true;
-    int i = 0;
-    for (int j = jlo; j < jhi && ok; ++j, ++i) {
-        const int ks = i % T::NSK, kn = i / T::NSK;
-        if (!mbar_wait(bar(Bars::K_EMPTY + ks), (kn & 1) ^ 1, ab, SITE_PROD_KEMPTY)) {
-            ok = false;
-            break;
+    int i = 0;  // K/V blocks loaded so far
+    for (int n = 0; ok && (T::PERSIST || n < 1); ++n) {
+        const int item = item_at(p, n);
+        if (item < 0) break;
+        const Item I = make_item<T>(p, item);
+        const Work& w = I.w;
+        const int nbox_v = I.dv / T::BOX;
+        for (int j = I.jlo; j < I.jhi; ++j, ++i) {
+            const int ks = i % T::NSK, kn = i / T::NSK;
+            if (!mbar_wait(bar(Bars::K_EMPTY + ks), (kn & 1) ^ 1, ab, SITE_PROD_KEMPTY)) {
+                ok = false;
+                break;
+            }
+            mbar_arrive_expect_tx(bar(Bars::K_FULL + ks), T::K_TILE);
+            const uint32_t kdst = smem_u32(smem + T::OFF_K + ks * T::K_TILE);
+            for (int bx = 0; bx < T::NBOX; ++bx)
+                tma_load_4d(kdst + bx * T::K_BOX_BYTES, tmK, bar(Bars::K_FULL + ks), bx * T::BOX, j * T::BC, w.kvh,
+                            w.b, pol_kv);
+            kfill[ks]++;
+            const int vs = i % T::NSV, vn = i / T::NSV;
+            if (!mbar_wait(bar(Bars::V_EMPTY + vs), (vn & 1) ^ 1, ab, SITE_PROD_VEMPTY)) {
+                ok = false;
+                break;
+            }
+            mbar_arrive_expect_tx(bar(Bars::V_FULL + vs), nbox_v * T::K_BOX_BYTES);
+            const uint32_t vdst = smem_u32(smem + T::OFF_V + vs * T::V_TILE);
+            for (int bx = 0; bx < nbox_v; ++bx)
+                tma_load_4d(vdst + bx * T::K_BOX_BYTES, tmV, bar(Bars::V_FULL + vs), I.dv0 + bx * T::BOX,
+                            j * T::BC, w.kvh, w.b, pol_kv);
+            vfill[vs]++;
         }
-        mbar_arrive_expect_tx(bar(Bars::K_FULL + ks), T::K_TILE);
-        const uint32_t kdst = smem_u32(smem + T::OFF_K + ks * T::K_TILE);
-        for (int bx = 0; bx < T::NBOX; ++bx)
-            tma_load_4d(kdst + bx * T::K_BOX_BYTES, tmK, bar(Bars::K_FULL + ks), bx * T::BOX, j * T::BC, w.kvh, w.b,
-                        pol_kv);
-        kfill[ks]++;
-        const int vs = i % T::NSV, vn = i / T::NSV;
-        if (!mbar_wait(bar(Bars::V_EMPTY + vs), (vn & 1) ^ 1, ab, SITE_PROD_VEMPTY)) {
-            ok = false;
-            break;
-        }
-        mbar_arrive_expect_tx(bar(Bars::V_FULL + vs), nbox_v * T::K_BOX_BYTES);
-        const uint32_t vdst = smem_u32(smem + T::OFF_V + vs * T::V_TILE);
-        for (int bx = 0; bx < nbox_v; ++bx)
-            tma_load_4d(vdst + bx * T::K_BOX_BYTES, tmV, bar(Bars::V_FULL + vs), dv0 + bx * T::BOX, j * T::BC, w.kvh,
-                        w.b, pol_kv);
-        vfill[vs]++;
     }
     if (!ok) {
         // unwind: let every issued copy land before the CTA can exit
-        mbar_wait_drain(bar(Bars::Q_FULL), 0);
         for (int s = 0; s < T::NSK; ++s)
             if (kfill[s] > 0) mbar_wait_drain(bar(Bars::K_FULL + s), (kfill[s] - 1) & 1);
         for (int s = 0; s < T::NSV; ++s)
@@ -776,80 +906,110 @@ __device__ __forceinline__ void issue_pv(const Descs<T>& dz, uint32_t tmem, int 
     }
 }
 
-// Double-buffered S: S(t, j) lives in buffer (j - ta[t]) & 1.  The prologue
-// issues QK for the first two blocks; block j then issues, per tile, PV(j)
-// (after P(t, j) is published) and QK(j+2) into the buffer PV(j) just read
-// (tcgen05 MMAs from one thread run in issue order).  The softmax of block
-// j+1 meanwhile works on the other buffer, so a tile's softmax never waits
-// for the tensor core except for S itself.
+// Double-buffered S: S(t, j) lives in buffer (g + j - ta[t]) & 1, g = blocks of
+// tile t in this CTA's earlier items.  Per item the prologue issues QK for the
+// first two blocks; block j then issues, per tile, PV(j) (after P(t, j) is
+// published) and QK(j+2) into the buffer PV(j) just read (tcgen05 MMAs from
+// one thread run in issue order).  The softmax of block j+1 meanwhile works
+// on the other buffer, so a tile's softmax never waits for the tensor core
+// except for S itself.  An item's first PV overwrites O, so it waits until the
+// epilogue of the tile's previous item has read O out of TMEM.
 template <class T>
-__device__ void mma_role_sdb(const Params& p, const Work& w, int jlo, int jhi, const int* ta, const int* te,
-                             uint8_t* smem, uint32_t tmem, const Abort& ab, int dv, int issuer) {
+__device__ void mma_role_sdb(const Params& p, uint8_t* smem, uint32_t tmem, const Abort& ab, int issuer) {
     // issuer i serves tiles [t_begin, t_end)
     const int t_begin = T::NI == 1 ? 0 : issuer;
     const int t_end = T::NI == 1 ? T::NT : issuer + 1;
     const uint32_t bars = smem_u32(smem);
     auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
-    const uint32_t idesc_pv = instr_desc(1u, 0u, 1u, BM, static_cast<uint32_t>(dv));
     const Descs<T> dz(smem);
-    bool ok = mbar_wait(bar(Bars::Q_FULL), 0, ab, SITE_MMA_Q);
-    tc_fence_after();
-    int kc = 0, vc = 0;
-    for (int jj = jlo; ok && jj < jhi && jj < jlo + 2; ++jj) {
-        const int ks = kc % T::NSK;
-        if (!mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+    int kc = 0, vc = 0, n = 0;
+    int g[2] = {0, 0}, n_o[2] = {0, 0};
+    bool ok = true;
+    for (; ok && (T::PERSIST || n < 1); ++n) {
+        const int item = item_at(p, n);
+        if (item < 0) break;
+        const Item I = make_item<T>(p, item);
+        const int* ta = I.ta;
+        const int* te = I.te;
+        const int jlo = I.jlo, jhi = I.jhi;
+        const uint32_t idesc_pv = instr_desc(1u, 0u, 1u, BM, static_cast<uint32_t>(I.dv));
+        if (!mbar_wait(bar(Bars::Q_FULL), n & 1, ab, SITE_MMA_Q)) {
             ok = false;
             break;
         }
         tc_fence_after();
-        for (int t = t_begin; t < t_end; ++t) {
-            if (ta[t] <= jj && jj < te[t]) {
-                const int sb = (jj - ta[t]) & 1;
-                issue_qk<T>(dz, tmem, t, ks, sb);
-                tc_commit(bar(Bars::S_FULL + t * T::NSB + sb));
+        for (int jj = jlo; jj < jhi && jj < jlo + 2; ++jj) {
+            const int ks = kc % T::NSK;
+            if (!mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+                ok = false;
+                break;
             }
-        }
-        tc_commit(bar(Bars::K_EMPTY + ks));
-        kc++;
-    }
-    for (int j = jlo; ok && j < jhi; ++j) {
-        const int vs = vc % T::NSV;
-        if (!mbar_wait(bar(Bars::V_FULL + vs), (vc / T::NSV) & 1, ab, SITE_MMA_V)) {
-            ok = false;
-            break;
-        }
-        const bool has_k = j + 2 < jhi;
-        const int ks = kc % T::NSK;
-        if (has_k && !mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
-            ok = false;
-            break;
-        }
-        tc_fence_after();
-        for (int t = t_begin; t < t_end; ++t) {
-            if (ta[t] <= j && j < te[t]) {
-                const int it = j - ta[t];
-                const int sb = it & 1;
-                if (!mbar_wait(bar(Bars::P_FULL + t * T::NSB + sb), (it >> 1) & 1, ab, SITE_MMA_P)) {
-                    ok = false;
-                    break;
+            tc_fence_after();
+            for (int t = t_begin; t < t_end; ++t) {
+                if (ta[t] <= jj && jj < te[t]) {
+                    const int sb = (g[t] + jj - ta[t]) & 1;
+                    issue_qk<T>(dz, tmem, t, ks, sb);
+                    tc_commit(bar(Bars::S_FULL + t * T::NSB + sb));
                 }
-                tc_fence_after();
-                issue_pv<T>(dz, tmem, t, vs, it > 0, idesc_pv, sb);
-                tc_commit(bar(Bars::PV_DONE + t));
-                if (j == te[t] - 1) tc_commit(bar(Bars::O_FULL + t));
             }
-            if (has_k && ta[t] <= j + 2 && j + 2 < te[t]) {
-                const int sb = (j + 2 - ta[t]) & 1;
-                issue_qk<T>(dz, tmem, t, ks, sb);
-                tc_commit(bar(Bars::S_FULL + t * T::NSB + sb));
+            tc_commit(bar(Bars::K_EMPTY + ks));
+            kc++;
+        }
+        // Q is released as soon as this issuer's last Q K^T of the item is
+        // issued (the commit fires when those MMAs complete), so the next
+        // item's Q loads while the last PVs run
+        if (ok && jhi - jlo <= 2) tc_commit(bar(Bars::Q_EMPTY));
+        for (int j = jlo; ok && j < jhi; ++j) {
+            const int vs = vc % T::NSV;
+            if (!mbar_wait(bar(Bars::V_FULL + vs), (vc / T::NSV) & 1, ab, SITE_MMA_V)) {
+                ok = false;
+                break;
+            }
+            const bool has_k = j + 2 < jhi;
+            const int ks = kc % T::NSK;
+            if (has_k && !mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            for (int t = t_begin; t < t_end; ++t) {
+                if (ta[t] <= j && j < te[t]) {
+                    const int it = j - ta[t];
+                    const int gg = g[t] + it;
+                    const int sb = gg & 1;
+                    if (!mbar_wait(bar(Bars::P_FULL + t * T::NSB + sb), (gg >> 1) & 1, ab, SITE_MMA_P)) {
+                        ok = false;
+                        break;
+                    }
+                    if (it == 0 && n_o[t] > 0 &&
+                        !mbar_wait(bar(Bars::O_EMPTY + t), (n_o[t] - 1) & 1, ab, SITE_MMA_OEMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv<T>(dz, tmem, t, vs, it > 0, idesc_pv, sb);
+                    tc_commit(bar(Bars::PV_DONE + t));
+                    if (j == te[t] - 1) tc_commit(bar(Bars::O_FULL + t));
+                }
+                if (has_k && ta[t] <= j + 2 && j + 2 < te[t]) {
+                    const int sb = (g[t] + j + 2 - ta[t]) & 1;
+                    issue_qk<T>(dz, tmem, t, ks, sb);
+                    tc_commit(bar(Bars::S_FULL + t * T::NSB + sb));
+                }
+            }
+            if (!ok) break;
+            tc_commit(bar(Bars::V_EMPTY + vs));
+            vc++;
+            if (has_k) {
+                tc_commit(bar(Bars::K_EMPTY + ks));
+                kc++;
+                if (j + 2 == jhi - 1) tc_commit(bar(Bars::Q_EMPTY));
             }
         }
         if (!ok) break;
-        tc_commit(bar(Bars::V_EMPTY + vs));
-        vc++;
-        if (has_k) {
-            tc_commit(bar(Bars::K_EMPTY + ks));
-            kc++;
+        for (int t = t_begin; t < t_end; ++t) {
+            g[t] += te[t] - ta[t];
+            n_o[t] += te[t] > ta[t] ? 1 : 0;
         }
     }
     tc_commit(bar(Bars::DRAIN + issuer));
@@ -857,69 +1017,91 @@ __device__ void mma_role_sdb(const Params& p, const Work& w, int jlo, int jhi, c
 }
 
 template <class T>
-__device__ void mma_role(const Params& p, const Work& w, int jlo, int jhi, const int* ta, const int* te,
-                         uint8_t* smem, uint32_t tmem, const Abort& ab, int dv) {
+__device__ void mma_role(const Params& p, uint8_t* smem, uint32_t tmem, const Abort& ab) {
     const uint32_t bars = smem_u32(smem);
     auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
-    const int kready = Bars::K_FULL;
-    const uint32_t idesc_pv = instr_desc(T::I8 ? 2u : 1u, T::I8 ? 1u : 0u, 1u, BM, static_cast<uint32_t>(dv));
     const Descs<T> dz(smem);
-    bool ok = mbar_wait(bar(Bars::Q_FULL), 0, ab, SITE_MMA_Q);
-    tc_fence_after();
-    int kc = 0, vc = 0;
-    int pc[2] = {0, 0};
-    if (ok && jlo < jhi) {
-        if (!mbar_wait(bar(kready + 0), 0, ab, SITE_MMA_K)) ok = false;
-        if (ok) {
-            tc_fence_after();
-            for (int t = 0; t < T::NT; ++t) {
-                if (ta[t] <= jlo && jlo < te[t]) {
-                    issue_qk<T>(dz, tmem, t, 0);
-                    tc_commit(bar(Bars::S_FULL + t));
-                }
-            }
-            tc_commit(bar(Bars::K_EMPTY + 0));
-            kc = 1;
-        }
-    }
-    for (int j = jlo; ok && j < jhi; ++j) {
-        const int vs = vc % T::NSV;
-        if (!mbar_wait(bar(Bars::V_FULL + vs), (vc / T::NSV) & 1, ab, SITE_MMA_V)) {
-            ok = false;
-            break;
-        }
-        const bool has_next = j + 1 < jhi;
-        const int ks = kc % T::NSK;
-        if (has_next && !mbar_wait(bar(kready + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+    int kc = 0, vc = 0, n = 0;
+    int pc[2] = {0, 0}, n_o[2] = {0, 0};
+    bool ok = true;
+    for (; ok && (T::PERSIST || n < 1); ++n) {
+        const int item = item_at(p, n);
+        if (item < 0) break;
+        const Item I = make_item<T>(p, item);
+        const int* ta = I.ta;
+        const int* te = I.te;
+        const int jlo = I.jlo, jhi = I.jhi;
+        const uint32_t idesc_pv =
+            instr_desc(T::I8 ? 2u : 1u, T::I8 ? 1u : 0u, 1u, BM, static_cast<uint32_t>(I.dv));
+        if (!mbar_wait(bar(Bars::Q_FULL), n & 1, ab, SITE_MMA_Q)) {
             ok = false;
             break;
         }
         tc_fence_after();
-        for (int t = 0; t < T::NT; ++t) {
-            const bool act = ta[t] <= j && j < te[t];
-            const bool act_next = has_next && ta[t] <= j + 1 && j + 1 < te[t];
-            if (act) {
-                if (!mbar_wait(bar(Bars::P_FULL + t), pc[t] & 1, ab, SITE_MMA_P)) {
-                    ok = false;
-                    break;
+        if (jlo < jhi) {
+            const int ks = kc % T::NSK;
+            if (!mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            for (int t = 0; t < T::NT; ++t) {
+                if (ta[t] <= jlo && jlo < te[t]) {
+                    issue_qk<T>(dz, tmem, t, ks);
+                    tc_commit(bar(Bars::S_FULL + t));
                 }
-                pc[t]++;
-                tc_fence_after();
-                issue_pv<T>(dz, tmem, t, vs, j > ta[t], idesc_pv);
-                if (j == te[t] - 1) tc_commit(bar(Bars::O_FULL + t));
             }
-            if (act_next) {
-                issue_qk<T>(dz, tmem, t, ks);
-                tc_commit(bar(Bars::S_FULL + t));
-            }
-        }
-        if (!ok) break;
-        tc_commit(bar(Bars::V_EMPTY + vs));
-        vc++;
-        if (has_next) {
             tc_commit(bar(Bars::K_EMPTY + ks));
             kc++;
         }
+        if (ok && jhi - jlo <= 1) tc_commit(bar(Bars::Q_EMPTY));  // last Q K^T of the item issued
+        for (int j = jlo; ok && j < jhi; ++j) {
+            const int vs = vc % T::NSV;
+            if (!mbar_wait(bar(Bars::V_FULL + vs), (vc / T::NSV) & 1, ab, SITE_MMA_V)) {
+                ok = false;
+                break;
+            }
+            const bool has_next = j + 1 < jhi;
+            const int ks = kc % T::NSK;
+            if (has_next && !mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            for (int t = 0; t < T::NT; ++t) {
+                const bool act = ta[t] <= j && j < te[t];
+                const bool act_next = has_next && ta[t] <= j + 1 && j + 1 < te[t];
+                if (act) {
+                    if (!mbar_wait(bar(Bars::P_FULL + t), pc[t] & 1, ab, SITE_MMA_P)) {
+                        ok = false;
+                        break;
+                    }
+                    pc[t]++;
+                    if (j == ta[t] && n_o[t] > 0 &&
+                        !mbar_wait(bar(Bars::O_EMPTY + t), (n_o[t] - 1) & 1, ab, SITE_MMA_OEMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv<T>(dz, tmem, t, vs, j > ta[t], idesc_pv);
+                    if (j == te[t] - 1) tc_commit(bar(Bars::O_FULL + t));
+                }
+                if (act_next) {
+                    issue_qk<T>(dz, tmem, t, ks);
+                    tc_commit(bar(Bars::S_FULL + t));
+                }
+            }
+            if (!ok) break;
+            tc_commit(bar(Bars::V_EMPTY + vs));
+            vc++;
+            if (has_next) {
+                tc_commit(bar(Bars::K_EMPTY + ks));
+                kc++;
+                if (j + 1 == jhi - 1) tc_commit(bar(Bars::Q_EMPTY));
+            }
+        }
+        if (!ok) break;
+        for (int t = 0; t < T::NT; ++t) n_o[t] += te[t] > ta[t] ? 1 : 0;
     }
     // drain: no MMA may still be writing TMEM when the CTA releases it
     tc_commit(bar(Bars::DRAIN));
@@ -965,6 +1147,11 @@ __global__ void __launch_bounds__(T::THREADS, 1)
             mbar_init(bar(Bars::EPI + t), 128);
             mbar_init(bar(Bars::EXPD + t), 4);
         }
+        mbar_init(bar(Bars::Q_EMPTY), T::NI);
+        for (int t = 0; t < T::NT; ++t) {
+            mbar_init(bar(Bars::O_EMPTY + t), 4);
+            mbar_init(bar(Bars::STG_FREE + t), 1);
+        }
         fence_barrier_init();
     }
     if (warp == T::WARP_MMA) {
@@ -977,25 +1164,6 @@ __global__ void __launch_bounds__(T::THREADS, 1)
     const uint32_t tmem = *tmem_slot;
     const Abort ab{abort_flag};
 
-    const Work w = decode_work<T>(p, blockIdx.x);
-    int dv = T::DVMAX, dv0 = 0;
-    if (p.n_split > 1) {
-        dv0 = w.split * p.dv_split;
-        dv = min(p.dv_split, T::D - dv0);
-    } else {
-        dv = T::D < T::DVMAX ? T::D : T::DVMAX;
-    }
-    int ta[2] = {0, 0}, te[2] = {0, 0};
-    for (int t = 0; t < T::NT; ++t) tile_blocks<T>(p, w.row0[t], w.valid[t], ta[t], te[t]);
-    int jlo = 1 << 30, jhi = -1;
-    for (int t = 0; t < T::NT; ++t) {
-        if (te[t] > ta[t]) {
-            jlo = min(jlo, ta[t]);
-            jhi = max(jhi, te[t]);
-        }
-    }
-    if (jhi < 0) jlo = jhi = 0;
-
     if constexpr (T::RESPLIT) {
         if (warp < 4 * T::NT)
             regs_increase<T::SOFTMAX_REGS>();
@@ -1003,22 +1171,25 @@ __global__ void __launch_bounds__(T::THREADS, 1)
             regs_decrease<T::CONTROL_REGS>();
     }
     if (warp < 4 * T::NT) {
-        softmax_role<T>(p, &tmO, w, warp / 4, smem, tmem, ab, dv, dv0);
+        softmax_role<T>(p, &tmO, warp / 4, smem, tmem, ab);
         tc_fence_before();
     } else if (warp == T::WARP_PROD) {
-        if (sm100::lane_id() == 0) producer_role<T>(p, &tmQ, &tmK, &tmV, w, jlo, jhi, smem, ab, dv, dv0);
+        if (sm100::lane_id() == 0) producer_kv_role<T>(p, &tmK, &tmV, smem, ab);
+        __syncwarp();
+    } else if (warp == T::WARP_QLOAD) {
+        if (sm100::lane_id() == 0) producer_q_role<T>(p, &tmQ, smem, ab);
         __syncwarp();
     } else if (warp == T::WARP_MMA) {
         if (sm100::lane_id() == 0) {
             if constexpr (T::SDB)
-                mma_role_sdb<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv, 0);
+                mma_role_sdb<T>(p, smem, tmem, ab, 0);
             else
-                mma_role<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv);
+                mma_role<T>(p, smem, tmem, ab);
         }
         __syncwarp();
     } else if (T::NI == 2 && warp == T::WARP_MMA + 1) {
         if constexpr (T::SDB) {
-            if (sm100::lane_id() == 0) mma_role_sdb<T>(p, w, jlo, jhi, ta, te, smem, tmem, ab, dv, 1);
+            if (sm100::lane_id() == 0) mma_role_sdb<T>(p, smem, tmem, ab, 1);
         }
         __syncwarp();
     }

@@ -20,6 +20,7 @@
 #include "fa_decode.cuh"
 #include "fa_prefill.cuh"
 #include "rope.cuh"
+#include "quant.cuh"
 
 namespace rdna {
 namespace {
@@ -170,9 +171,25 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
         items = static_cast<int64_t>(p.n_rp) * c.B * c.H;
     items *= p.n_split;
     if (items > INT32_MAX) return fail(err, "problem too large for one launch");
+    p.n_items = static_cast<int>(items);
+
+    // Persistent kernels: one CTA per SM, each looping over items i, i + grid, ...
+    // (the item order is longest-first, so the strided split stays balanced).
+    // Their shared-memory request is at least half the SM's, so two CTAs never
+    // share an SM (and its 512 TMEM columns).
+    int64_t grid = items;
+    int smem_bytes = T::SMEM_BYTES;
+    if constexpr (T::PERSIST) {
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (grid > sms) grid = sms;
+        constexpr int kHalfSm = 116 * 1024;
+        if (smem_bytes < kHalfSm) smem_bytes = kHalfSm;
+    }
 
     auto kern = fa_prefill_kernel<T>;
-    cudaError_t ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM_BYTES);
+    cudaError_t ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
     if constexpr (T::RESPLIT) {
         // setmaxnreg.inc waits for registers the CTA was launched with: refuse to
@@ -184,7 +201,7 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
             return fail(err, "internal: kernel register count does not match its register split");
     }
 
-    kern<<<static_cast<unsigned>(items), T::THREADS, T::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, tmO, p);
+    kern<<<static_cast<unsigned>(grid), T::THREADS, smem_bytes, stream>>>(tmQ, tmK, tmV, tmO, p);
     ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
     return 0;
@@ -197,7 +214,8 @@ int dispatch_f16_dim(char* err, const Common& c, const prefill::Params& p, cudaS
     if constexpr (D <= 128) {
         // two 128-row tiles per CTA, 64-key blocks, S double-buffered in TMEM
         // (2 tiles x 2 buffers x 64 columns + 2 x D columns of O <= 512)
-        constexpr int stages = D <= 64 ? 6 : D <= 96 ? 5 : 4;
+        // persistent kernels give shared memory to a separate O staging buffer
+        constexpr int stages = D <= 64 ? 6 : D <= 96 ? 5 : (RDNA_PERSIST ? 3 : 4);
         return launch_prefill<Traits<D, D, 64, 2, stages, stages, false, true>>(err, c, p, st, dt);
     } else if constexpr (D <= 256) {
         // one tile per CTA (TMEM holds one O of up to 256 columns), 64-key blocks
@@ -510,11 +528,65 @@ int forwardInt8QK(const ForwardParamsInt8QK& a, void* stream) {
     p.pv_scale = a.vScale / 127.0f;
     p.q_vec = static_cast<const float*>(a.qScaleVec);
     p.k_vec = static_cast<const float*>(a.kScaleVec);
+    p.v_chan = static_cast<const float*>(a.vChannel);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     constexpr CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
     if (a.headDim == 64)
         return launch_prefill<prefill::Traits<64, 64, 128, 2, 4, 4, true>>(g_err_i8, c, p, st, dt);
     return launch_prefill<prefill::Traits<128, 128, 128, 1, 3, 3, true>>(g_err_i8, c, p, st, dt);
+}
+
+int quantizeInt8QKV(const QuantizeInt8Params& a, void* stream) {
+    if (a.q == nullptr || a.k == nullptr || a.v == nullptr || a.qInt8 == nullptr || a.kInt8 == nullptr ||
+        a.vInt8 == nullptr || a.qScale == nullptr || a.kScale == nullptr || a.vChannel == nullptr)
+        return fail(g_err_i8, "null tensor pointer");
+    if (a.batchSize == 0 || a.numHeads == 0 || a.seqLen == 0 || a.keySeqLen == 0) return fail(g_err_i8, "empty problem");
+    if (a.numKvHeads == 0 || a.numHeads % a.numKvHeads != 0)
+        return fail(g_err_i8, "numHeads must be a positive multiple of numKvHeads");
+    if (a.headDim != 64 && a.headDim != 128)
+        return fail(g_err_i8, "unsupported head_dim (only 64 and 128 are compiled in for the int8 kernel)");
+    auto aligned = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; };
+    if (!aligned(a.q, 16) || !aligned(a.k, 16) || !aligned(a.v, 16) || !aligned(a.qInt8, 8) || !aligned(a.kInt8, 8) ||
+        !aligned(a.vInt8, 8) || !aligned(a.qScale, 4) || !aligned(a.kScale, 4) || !aligned(a.vChannel, 4))
+        return fail(g_err_i8, "tensor base pointers must be 16-byte aligned (int8 outputs 8, scales 4)");
+    const int64_t st[9] = {a.qStrideB, a.qStrideH, a.qStrideS, a.kStrideB, a.kStrideH, a.kStrideS,
+                           a.vStrideB, a.vStrideH, a.vStrideS};
+    for (int64_t x : st)
+        if (x <= 0 || x % 8 != 0) return fail(g_err_i8, "strides must be positive multiples of 16 bytes");
+    const int64_t qrows = static_cast<int64_t>(a.batchSize) * a.numHeads * a.seqLen;
+    const int64_t krows = static_cast<int64_t>(a.batchSize) * a.numKvHeads * a.keySeqLen;
+    const int64_t units = static_cast<int64_t>(a.batchSize) * a.numKvHeads;
+    quant::Params p{};
+    p.t[0] = quant::Rows{static_cast<const __half*>(a.q), static_cast<int8_t*>(a.qInt8), static_cast<float*>(a.qScale),
+                         a.qStrideB, a.qStrideH, a.qStrideS, static_cast<int>(a.numHeads), static_cast<int>(a.seqLen),
+                         qrows};
+    p.t[1] = quant::Rows{static_cast<const __half*>(a.k), static_cast<int8_t*>(a.kInt8), static_cast<float*>(a.kScale),
+                         a.kStrideB, a.kStrideH, a.kStrideS, static_cast<int>(a.numKvHeads),
+                         static_cast<int>(a.keySeqLen), krows};
+    p.v = static_cast<const __half*>(a.v);
+    p.vi = static_cast<int8_t*>(a.vInt8);
+    p.vch = static_cast<float*>(a.vChannel);
+    p.vsb = a.vStrideB;
+    p.vsh = a.vStrideH;
+    p.vss = a.vStrideS;
+    p.Hkv = static_cast<int>(a.numKvHeads);
+    p.KS = static_cast<int>(a.keySeqLen);
+    p.D = static_cast<int>(a.headDim);
+    // per-token part: enough warps to cover every row a few times over the SMs
+    const int rows_per_block = (quant::kThreads / 32) * (32 / (p.D / 8));
+    auto blocks_for = [&](int64_t rows) {
+        const int64_t want = (rows + rows_per_block - 1) / rows_per_block;
+        return static_cast<int>(want < 148 * 8 ? want : 148 * 8);
+    };
+    p.blocks_q = blocks_for(qrows);
+    p.blocks_k = blocks_for(krows);
+    const int64_t grid = static_cast<int64_t>(p.blocks_q) + p.blocks_k + units;
+    if (grid > INT32_MAX) return fail(g_err_i8, "problem too large for one launch");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    quant::quantize_qkv_kernel<<<static_cast<unsigned>(grid), quant::kThreads, 0, s>>>(p);
+    const cudaError_t ce = cudaGetLastError();
+    if (ce != cudaSuccess) return fail(g_err_i8, "%s", cudaGetErrorString(ce));
+    return 0;
 }
 
 const char* lastError() { return g_err_f16[0] ? g_err_f16 : nullptr; }

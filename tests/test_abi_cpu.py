@@ -152,3 +152,15 @@ def test_workspace_size_is_the_rotated_q_and_k():
     assert ws(4, 32, 8, 4096, 4096, 128, 1) == 4 * 32 * 4096 * 128 * 2 + 4 * 8 * 4096 * 128 * 2
     assert ws(1, 3, 1, 5, 7, 32, 1) == 1024 + 512  # 960 and 448 bytes, each rounded up to a multiple of 256
     assert ws(4, 32, 8, 4096, 4096, 128, 0) == 0
+
+
+def test_int8_quantize_argument_errors():
+    lib = R._lib_handle()
+    f = lib.rdna_int8_quantize_qkv
+    ok_strides = (8 * 64 * 64, 64 * 64, 64) * 3
+    rc = f(None, 16, 16, *ok_strides, 1, 8, 8, 64, 64, 64, 16, 16, 16, 16, 16, 16, None)
+    assert rc == -3 and "null tensor pointer" in lib.rdna_get_error().decode()
+    rc = f(16, 16, 16, *ok_strides, 1, 8, 8, 64, 64, 96, 16, 16, 16, 16, 16, 16, None)
+    assert rc == -3 and "unsupported head_dim" in lib.rdna_get_error().decode()
+    rc = f(16, 16, 16, *ok_strides, 1, 8, 3, 64, 64, 64, 16, 16, 16, 16, 16, 16, None)
+    assert rc == -3 and "multiple of numKvHeads" in lib.rdna_get_error().decode()

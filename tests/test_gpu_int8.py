@@ -96,3 +96,53 @@ def test_int8_strided_kv():
     assert rc == 0, lib.rdna_get_error()
     ref = c_oracle.attention_int8(qi, ki, vi, qs, ks, vs)
     assert rel_rms(out.cpu(), ref) < 5e-2
+
+
+def _two_step_quantized(q, k, v, causal=False, window=-1):
+    """The reference's flash_attn_int8qk_quantized (rdnattention/__init__.py:346-357):
+    host-side torch quantisation, the INT8 kernel, then the per-channel V rescale of
+    the fp16 output.  The reference broadcasts the (B, Hkv, D) scale against the
+    (B, H, S, D) output, which only works for H == Hkv; here each KV head's scale is
+    repeated over its query heads, which is what the fused kernel applies."""
+    _, _, vi, _, _, v_scale, vch = R.quantize_int8_perchannel_v(q, k, v)
+    qi, ki, qs, ks = R.quantize_int8_qk_pertoken(q, k)
+    out = R.flash_attn_int8qk(qi.contiguous(), ki.contiguous(), vi.contiguous(), qs, ks, v_scale, causal, window)
+    vch = vch.repeat_interleave(q.shape[1] // k.shape[1], dim=1)
+    return (out.float() * vch.unsqueeze(-2)).to(out.dtype)
+
+
+@pytest.mark.parametrize("B,H,Hkv,S,KS,D", [(2, 8, 2, 300, 517, 64), (1, 4, 4, 256, 256, 128),
+                                            (3, 6, 3, 33, 1000, 128)])
+def test_device_quantization_bit_exact(B, H, Hkv, S, KS, D):
+    """rdna_int8_quantize_qkv == quantize_int8_qk_pertoken + quantize_int8_perchannel_v,
+    byte for byte, on strided K/V views ([B, KS, Hkv, D] storage), with an all-zero Q
+    row and an all-zero V column (scale 1 paths)."""
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + S)
+    q = (torch.randn(B, H, S, D, generator=g, device="cuda") * 3).half()
+    k = torch.randn(B, KS, Hkv, D, generator=g, device="cuda").half().transpose(1, 2)
+    v = (torch.randn(B, KS, Hkv, D, generator=g, device="cuda") * 0.5).half().transpose(1, 2)
+    q[0, 0, 0] = 0
+    v[0, 0, :, 5] = 0
+    qi, ki, vi, qs, ks, vch = R.quantize_int8_qkv(q, k, v)
+    rqi, rki, rqs, rks = R.quantize_int8_qk_pertoken(q, k)
+    _, _, rvi, _, _, _, rvch = R.quantize_int8_perchannel_v(q, k, v)
+    for name, a, b in (("q_scale", qs, rqs), ("k_scale", ks, rks), ("v_channel", vch, rvch),
+                       ("qi", qi, rqi), ("ki", ki, rki), ("vi", vi, rvi)):
+        bad = (a != b.to(a.dtype)).nonzero()
+        assert bad.numel() == 0, f"{name}: {bad.shape[0]} mismatches, first at {bad[0].tolist()}"
+    assert qs[0, 0, 0].item() == 1.0 and vch[0, 0, 5].item() == 1.0
+
+
+@pytest.mark.parametrize("D,causal,window", [(64, False, -1), (128, True, -1), (64, True, 300)])
+def test_fused_vchannel_matches_two_step(D, causal, window):
+    """Device quantisation + per-channel V scale in the epilogue vs the reference's
+    host-side two-step path: the same arithmetic except that the fused path rounds
+    to fp16 once instead of twice (2 fp16 ulps relative + 1e-3 absolute)."""
+    B, H, Hkv, S, KS = 2, 8, 4, 700, 700
+    g = torch.Generator(device="cuda").manual_seed(D + int(causal))
+    q = torch.randn(B, H, S, D, generator=g, device="cuda").half()
+    k = torch.randn(B, Hkv, KS, D, generator=g, device="cuda").half()
+    v = (torch.randn(B, Hkv, KS, D, generator=g, device="cuda") * 2).half()
+    got = R.flash_attn_int8qk_quantized(q, k, v, causal, window)
+    ref = _two_step_quantized(q, k, v, causal, window)
+    torch.testing.assert_close(got.float(), ref.float(), rtol=2e-3, atol=1e-3)
