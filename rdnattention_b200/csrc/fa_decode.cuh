@@ -20,6 +20,13 @@
 // The bound is HBM: per 32-key tile the warp moves 16 KB (D = 128) and
 // issues 64 MMAs, far below the tensor and issue limits, so the mma.sync
 // form costs nothing here while keeping the fragment-level softmax simple.
+//
+// RoPE (interleaved pairs, reference src/rdna/fa2_forward_f16.hip:63-77, Q
+// row position = its index s within the sequence, K position = key index):
+// Q is rotated as its fragments are loaded; each K tile is rotated in place in
+// shared memory by the warp that consumes it (lane = key row, fp32 math,
+// fp16 result), with the first table loads issued before the tile arrives.
+// The KV cache is read once, as without RoPE; the cos/sin rows come from L2.
 #pragma once
 
 #include <cuda.h>
@@ -56,7 +63,28 @@ struct Params {
     int causal;
     int window;
     float scale_log2;
+    int rope;               // nonzero: rotate Q and K (tables [max(S, KS), D/2] fp32)
+    const float* rope_cos;
+    const float* rope_sin;
 };
+
+// (x[2i], x[2i+1]) -> (a*c - b*s, a*s + b*c), fp32, rounded to fp16
+__device__ __forceinline__ uint32_t rotate_pair(uint32_t v, float c, float s) {
+    const __half2 h2 = *reinterpret_cast<const __half2*>(&v);
+    const float a = __low2float(h2), b = __high2float(h2);
+    const __half2 r = __floats2half2_rn(a * c - b * s, a * s + b * c);
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// One 16-byte chunk (4 pairs) of a key row, in place.
+__device__ __forceinline__ void rotate_chunk(uint8_t* ptr, const float4& c, const float4& s) {
+    uint4 x = *reinterpret_cast<const uint4*>(ptr);
+    x.x = rotate_pair(x.x, c.x, s.x);
+    x.y = rotate_pair(x.y, c.y, s.y);
+    x.z = rotate_pair(x.z, c.z, s.z);
+    x.w = rotate_pair(x.w, c.w, s.w);
+    *reinterpret_cast<uint4*>(ptr) = x;
+}
 
 template <int D>
 struct Layout {
@@ -245,6 +273,10 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
                     const int r = rows[ri];
                     const int h = kvh * p.G + r / p.S, s = r % p.S;
                     v = *reinterpret_cast<const uint32_t*>(p.q + b * p.qsb + h * p.qsh + s * p.qss + dc);
+                    if (p.rope) {
+                        const int64_t ti = static_cast<int64_t>(s) * (D / 2) + dc / 2;
+                        v = rotate_pair(v, __ldg(p.rope_cos + ti), __ldg(p.rope_sin + ti));
+                    }
                 }
                 qa[kk][j] = v;
             }
@@ -257,8 +289,22 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         const float sl2 = p.scale_log2;
         bool aborted = false;
 
+        constexpr int NCH = D / 8;                // 16-byte chunks per key row
+        constexpr int RG = NCH < 8 ? NCH : 8;     // chunks per table-load group
         for (int i = warp; i < ntiles; i += NCW) {
             const int s = i % NST, n = i / NST;
+            const int k0 = (t_begin + i) * KT;
+            // RoPE: this lane's key row; its first table group loads while the tile is in flight
+            const int rkey = k0 + lane;
+            const bool rrow = p.rope && rkey < p.KS;  // rows past KS are zero fill
+            float4 rc[RG], rs[RG];
+            if (rrow) {
+#pragma unroll
+                for (int u = 0; u < RG; ++u) {
+                    rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + static_cast<int64_t>(rkey) * (D / 2) + 4 * u));
+                    rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + static_cast<int64_t>(rkey) * (D / 2) + 4 * u));
+                }
+            }
             bool ok = !aborted && mbar_wait(full_bar(s), n & 1, ab, 0x502);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
@@ -267,7 +313,25 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
             }
             const uint32_t kb = smem_u32(ring + s * L::STAGE);
             const uint32_t vb = kb + L::TILE;
-            const int k0 = (t_begin + i) * KT;
+            if (p.rope) {
+                uint8_t* ktile = ring + s * L::STAGE;
+                if (rrow) {
+#pragma unroll
+                    for (int g0 = 0; g0 < NCH; g0 += RG) {
+                        if (g0 > 0) {
+#pragma unroll
+                            for (int u = 0; u < RG; ++u) {
+                                const int64_t ti = static_cast<int64_t>(rkey) * (D / 2) + 4 * (g0 + u);
+                                rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + ti));
+                                rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + ti));
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < RG; ++u) rotate_chunk(ktile + tile_off<D>(lane, g0 + u), rc[u], rs[u]);
+                    }
+                }
+                __syncwarp();  // every row rotated before ldmatrix reads across rows
+            }
 
             // S = Q K^T over 32 keys: 4 n-tiles of 8 keys
             float sc[4][4];
@@ -349,6 +413,9 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
                     mma16816(oacc[2 * dp + 1], pa[kk2], b2, b3);
                 }
             }
+            // the K rows rewritten by this warp (generic proxy) are ordered before the
+            // next TMA write into the slot (async proxy)
+            if (p.rope) fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(empty_bar(s));
         }

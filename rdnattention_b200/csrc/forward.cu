@@ -237,9 +237,11 @@ constexpr size_t kWsAlign = 256;
 
 size_t align_up(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
 
-// Workspace of an FP16 call: rotated Q and K (contiguous fp16) when RoPE is on.
+// Workspace of an FP16 call: rotated Q and K (contiguous fp16) when RoPE is on
+// and the call takes the prefill path (the decode kernel rotates in place).
 size_t f16_workspace_bytes(const ForwardParams& a) {
     if (!a.hasRope) return 0;
+    if (a.numKvHeads != 0 && decode::eligible(a.seqLen, a.numHeads / a.numKvHeads, a.headDim)) return 0;
     const size_t q = static_cast<size_t>(a.batchSize) * a.numHeads * a.seqLen * a.headDim * 2;
     const size_t k = static_cast<size_t>(a.batchSize) * a.numKvHeads * a.keySeqLen * a.headDim * 2;
     return align_up(q) + align_up(k);
@@ -352,6 +354,9 @@ int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
     p.causal = a.causal ? 1 : 0;
     p.window = a.windowSize > 0 ? a.windowSize : 0;
     p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.rope = a.hasRope ? 1 : 0;
+    p.rope_cos = static_cast<const float*>(a.rot_cos);
+    p.rope_sin = static_cast<const float*>(a.rot_sin);
 
     CUtensorMap tmK, tmV;
     const bool nokv = a.keySeqLen == 0;
@@ -425,6 +430,8 @@ int forwardF16Ws(const ForwardParams& a, void* workspace, size_t workspace_bytes
     Common c = f16_common(a);
     if (int rc = f16_validate(c, a)) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // small seq_len x group: the split-KV decode kernel (RoPE applied in place)
+    if (decode::eligible(a.seqLen, a.numHeads / a.numKvHeads, a.headDim)) return decode::launch_f16(g_err_f16, a, st);
     const size_t need = f16_workspace_bytes(a);
     if (need > 0) {
         if (workspace == nullptr || workspace_bytes < need)
@@ -432,8 +439,6 @@ int forwardF16Ws(const ForwardParams& a, void* workspace, size_t workspace_bytes
         if (reinterpret_cast<uintptr_t>(workspace) & (kWsAlign - 1))
             return fail(g_err_f16, "workspace must be 256-byte aligned");
         if (int rc = launch_rope(a, c, workspace, st)) return rc;
-    } else if (decode::eligible(a.seqLen, a.numHeads / a.numKvHeads, a.headDim)) {
-        return decode::launch_f16(g_err_f16, a, st);
     }
     return f16_attention(a, c, st);
 }

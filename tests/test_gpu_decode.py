@@ -1,11 +1,13 @@
-"""Split-KV decode path (seq_len * GQA group <= 16 rows, head_dim 64/128, no
-RoPE) vs the fp64 oracle.  Tolerance: max-abs <= 2e-3 and mean-abs <= 2e-4
-(the north-star FP16 gate), rel_rms < 3e-3 (tests/head_dim.py:49)."""
+"""Split-KV decode path (seq_len * GQA group <= 16 rows, head_dim 64/128, with
+or without RoPE) vs the fp64 oracle.  Tolerance: max-abs <= 2e-3 and mean-abs
+<= 2e-4 (the north-star FP16 gate), rel_rms < 3e-3 (tests/head_dim.py:49).
+With RoPE the oracle rounds the rotated Q/K to fp16 as the reference kernel
+does (src/rdna/fa2_forward_f16.hip:74-75)."""
 import numpy as np
 import pytest
 import torch
 
-from cases import rel_rms
+from cases import rel_rms, rope_tables
 from oracle import c_oracle
 
 pytestmark = pytest.mark.gpu
@@ -83,3 +85,23 @@ def test_decode_full_config5_sampled():
             _check(out[b:b + 1, h:h + 1].cpu(), ref)
     del kb, vb
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("B,H,Hkv,S,KS,D,causal,window,theta", [
+    (2, 32, 8, 1, 4096, 128, False, -1, 500000.0),  # GQA decode step, BASELINE config 2 theta
+    (2, 8, 2, 4, 1000, 64, True, -1, 10000.0),      # few tokens, causal, D=64
+    (1, 16, 1, 1, 3000, 128, False, 512, 1e6),      # MQA, two-sided window
+    (1, 4, 4, 1, 33, 128, False, -1, 10000.0),      # key tail (zero-filled rows past KS)
+])
+def test_decode_rope_vs_oracle(B, H, Hkv, S, KS, D, causal, window, theta):
+    """RoPE inside the decode kernel: Q at its row position, each K row at its
+    key position (reference semantics, no delta shift), cache read once."""
+    g = torch.Generator().manual_seed(B * 77 + KS)
+    q = torch.randn(B, H, S, D, generator=g).half()
+    kb, vb = _cache(B, Hkv, KS, D, g)
+    cos, sin = rope_tables(max(S, KS), D, theta)
+    got = R.flash_attn_strided(q.cuda(), kb.cuda().transpose(1, 2), vb.cuda().transpose(1, 2), is_causal=causal,
+                               window_size=window, rot_cos=cos.cuda(), rot_sin=sin.cuda()).cpu()
+    ref = c_oracle.attention_f16(q, kb.transpose(1, 2), vb.transpose(1, 2), causal=causal, window=window,
+                                 rot_cos=cos, rot_sin=sin, rope_round=True)
+    _check(got, ref)
