@@ -1,10 +1,14 @@
-// Split-KV decode kernel (seq_len small: G * seq_len <= 16 query rows per KV
+// Split-KV decode kernel (seq_len small: G * seq_len <= 64 query rows per KV
 // head), FP16, HBM-bound.
 //
 // Work unit = (batch b, kv head). All G = H / Hkv query heads of the group
-// and all seq_len query rows form the M = 16 rows of one m16n8k16 tile, so
-// every K/V byte read from HBM serves the whole group (the reference re-reads
-// K/V once per query head: src/rdna/fa2_forward_f16.hip:643-648).
+// and all seq_len query rows form the rows of the unit; each row group of 16
+// is the M = 16 of one m16n8k16 tile, so every K/V byte read from HBM serves
+// 16 rows (the reference re-reads K/V once per query head:
+// src/rdna/fa2_forward_f16.hip:643-648).  Units with more than 16 rows run
+// one cluster per row group, each streaming the unit's K/V (measured: the
+// time grows with the number of row groups; reading a tile once for all
+// groups needs the groups inside one CTA).
 //
 // A cluster of CS CTAs (1..8) splits the unit's visible key range.  Per CTA:
 //   warp 4       TMA producer: 32-key K and V tiles (strided [B, KS, Hkv, D]
@@ -50,7 +54,8 @@ constexpr int NCW = 4;         // consumer warps
 constexpr int NST = 8;
 static_assert(NST % NCW == 0, "each ring slot needs a single consumer warp");
 constexpr int THREADS = 32 * (NCW + 1);
-constexpr int MAX_ROWS = 16;   // G * seq_len per unit
+constexpr int MAX_ROWS = 16;   // rows per row group (one m16 tile)
+constexpr int MAX_RG = 4;      // row groups per unit: G * seq_len <= 64
 constexpr int MAX_CLUSTER = 8;
 
 struct Params {
@@ -59,6 +64,7 @@ struct Params {
     int64_t qsb, qsh, qss;
     int64_t osb, osh, oss;
     int B, H, Hkv, S, KS, G, R;  // R = G * S rows per unit
+    int NRG;                     // row groups per unit (ceil(R / 16))
     int delta;
     int causal;
     int window;
@@ -182,8 +188,10 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
     const Abort ab{abort_flag};
     uint8_t* ring = smem + L::OFF_RING;
 
-    const int unit = blockIdx.y;
+    const int unit = blockIdx.y / p.NRG, rg = blockIdx.y % p.NRG;
     const int b = unit / p.Hkv, kvh = unit % p.Hkv;
+    const int row0 = rg * MAX_ROWS;                   // first unit row of this row group
+    const int nrows = min(MAX_ROWS, p.R - row0);      // rows of this row group
     const uint32_t rank = cluster_rank(), csize = cluster_size();
 
     // visible key range of the unit (union over its rows), split across the cluster
@@ -248,7 +256,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         // ------------------------------------------------------------ consumers
         const int g = lane >> 2, t = lane & 3;
         // rows g and g + 8 of the 16-row tile: row r -> (head kvh*G + r / S, position r % S)
-        const int rows[2] = {g, g + 8};
+        const int rows[2] = {row0 + g, row0 + g + 8};  // unit rows
         int klo[2], khi[2];
         bool rvalid[2];
         for (int i = 0; i < 2; ++i) {
@@ -430,7 +438,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         float* wp = part + warp * L::WARP_PART;
 #pragma unroll
         for (int ri = 0; ri < 2; ++ri) {
-            const int r = rows[ri];
+            const int r = rows[ri] - row0;  // row within the group
 #pragma unroll
             for (int i2 = 0; i2 < D / 8; ++i2) {
                 wp[r * (D + 2) + 8 * i2 + 2 * t] = oacc[i2][2 * ri];
@@ -443,7 +451,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         }
         named_bar_sync(1, 32 * NCW);
         // combine the 4 warp partials into the CTA partial
-        for (int idx = threadIdx.x; idx < p.R * D; idx += 32 * NCW) {
+        for (int idx = threadIdx.x; idx < nrows * D; idx += 32 * NCW) {
             const int r = idx / D, d = idx % D;
             float M = -INFINITY;
             for (int w = 0; w < NCW; ++w) M = fmaxf(M, part[w * L::WARP_PART + r * (D + 2) + D]);
@@ -466,7 +474,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
     cluster_sync_all();
     if (rank == 0 && warp < NCW) {
         const uint32_t cta_base = smem_u32(cta);
-        for (int idx = threadIdx.x; idx < p.R * (D / 8); idx += 32 * NCW) {
+        for (int idx = threadIdx.x; idx < nrows * (D / 8); idx += 32 * NCW) {
             const int r = idx / (D / 8), c8 = idx % (D / 8);
             float M = -INFINITY;
             for (uint32_t cr = 0; cr < csize; ++cr)
@@ -487,7 +495,8 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
             v.y = pack_half2(o[2] * inv, o[3] * inv);
             v.z = pack_half2(o[4] * inv, o[5] * inv);
             v.w = pack_half2(o[6] * inv, o[7] * inv);
-            const int h = kvh * p.G + r / p.S, s = r % p.S;
+            const int ur = row0 + r;  // unit row
+            const int h = kvh * p.G + ur / p.S, s = ur % p.S;
             if (!*abort_flag)
                 *reinterpret_cast<uint4*>(p.o + b * p.osb + h * p.osh + s * p.oss + 8 * c8) = v;
         }
@@ -498,7 +507,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
 
 // ------------------------------------------------------------------ host
 inline bool eligible(uint32_t seq_len, uint32_t group, uint32_t head_dim) {
-    return (head_dim == 64 || head_dim == 128) && static_cast<uint64_t>(seq_len) * group <= MAX_ROWS;
+    return (head_dim == 64 || head_dim == 128) && static_cast<uint64_t>(seq_len) * group <= MAX_ROWS * MAX_RG;
 }
 
 int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream);

@@ -152,9 +152,10 @@ def test_workspace_size_is_the_rotated_q_and_k():
     assert ws(4, 32, 8, 4096, 4096, 128, 1) == 4 * 32 * 4096 * 128 * 2 + 4 * 8 * 4096 * 128 * 2
     assert ws(1, 3, 1, 5, 7, 32, 1) == 1024 + 512  # 960 and 448 bytes, each rounded up to a multiple of 256
     assert ws(4, 32, 8, 4096, 4096, 128, 0) == 0
-    # decode-shaped problems (seq_len * group <= 16, head_dim 64/128) rotate in place: no workspace
+    # decode-shaped problems (seq_len * group <= 64, head_dim 64/128) rotate in place: no workspace
     assert ws(64, 64, 8, 1, 32768, 128, 1) == 0
-    assert ws(64, 64, 8, 3, 32768, 128, 1) > 0  # 24 rows per KV head: prefill path
+    assert ws(64, 64, 8, 8, 32768, 128, 1) == 0  # 64 rows per KV head: four row groups
+    assert ws(64, 64, 8, 9, 32768, 128, 1) > 0   # 72 rows per KV head: prefill path
 
 
 def test_int8_quantize_argument_errors():

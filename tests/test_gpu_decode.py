@@ -1,5 +1,5 @@
-"""Split-KV decode path (seq_len * GQA group <= 16 rows, head_dim 64/128, with
-or without RoPE) vs the fp64 oracle.  Tolerance: max-abs <= 2e-3 and mean-abs
+"""Split-KV decode path (seq_len * GQA group <= 64 rows in row groups of 16,
+head_dim 64/128, with or without RoPE) vs the fp64 oracle.  Tolerance: max-abs <= 2e-3 and mean-abs
 <= 2e-4 (the north-star FP16 gate), rel_rms < 3e-3 (tests/head_dim.py:49).
 With RoPE the oracle rounds the rotated Q/K to fp16 as the reference kernel
 does (src/rdna/fa2_forward_f16.hip:74-75)."""
@@ -47,6 +47,9 @@ def _check(got, ref):
     (2, 8, 2, 1, 4096, 64, False, 512),      # two-sided window
     (1, 4, 4, 1, 33, 128, False, -1),        # tiny: one CTA, two tiles
     (1, 4, 2, 1, 1, 128, False, -1),         # single key
+    (2, 32, 4, 4, 2000, 128, True, -1),      # 32 rows per KV head: two row groups
+    (1, 16, 1, 4, 3000, 64, False, 512),     # 64 rows: four row groups, window
+    (2, 24, 4, 3, 777, 128, True, 100),      # 18 rows: a full and a 2-row group
 ])
 def test_decode_vs_oracle(B, H, Hkv, S, KS, D, causal, window):
     g = torch.Generator().manual_seed(B * 1000 + KS)
@@ -92,6 +95,7 @@ def test_decode_full_config5_sampled():
     (2, 8, 2, 4, 1000, 64, True, -1, 10000.0),      # few tokens, causal, D=64
     (1, 16, 1, 1, 3000, 128, False, 512, 1e6),      # MQA, two-sided window
     (1, 4, 4, 1, 33, 128, False, -1, 10000.0),      # key tail (zero-filled rows past KS)
+    (2, 16, 2, 3, 1500, 128, True, -1, 500000.0),   # 24 rows per KV head: two row groups
 ])
 def test_decode_rope_vs_oracle(B, H, Hkv, S, KS, D, causal, window, theta):
     """RoPE inside the decode kernel: Q at its row position, each K row at its
