@@ -5,10 +5,10 @@
 // and all seq_len query rows form the rows of the unit; each row group of 16
 // is the M = 16 of one m16n8k16 tile, so every K/V byte read from HBM serves
 // 16 rows (the reference re-reads K/V once per query head:
-// src/rdna/fa2_forward_f16.hip:643-648).  Units with more than 16 rows run
-// one cluster per row group, each streaming the unit's K/V (measured: the
-// time grows with the number of row groups; reading a tile once for all
-// groups needs the groups inside one CTA).
+// src/rdna/fa2_forward_f16.hip:643-648).  Units with more than 16 rows have
+// NRG = 2 or 4 row groups inside the CTA: warp w takes row group w % NRG, and
+// each K/V tile is consumed by NRG warps (one per group), so the cache is
+// still read once per unit.
 //
 // A cluster of CS CTAs (1..8) splits the unit's visible key range.  Per CTA:
 //   warp 4       TMA producer: 32-key K and V tiles (strided [B, KS, Hkv, D]
@@ -64,7 +64,7 @@ struct Params {
     int64_t qsb, qsh, qss;
     int64_t osb, osh, oss;
     int B, H, Hkv, S, KS, G, R;  // R = G * S rows per unit
-    int NRG;                     // row groups per unit (ceil(R / 16))
+    int NRG;                     // row groups per unit: 1, 2 or 4 (divides the consumer warps)
     int delta;
     int causal;
     int window;
@@ -103,7 +103,7 @@ struct Layout {
     static constexpr int SMEM_BYTES = OFF_RING + NST * STAGE + 1024;  // + align slack
     // after the loop the ring is reused for partials
     static constexpr int WARP_PART = MAX_ROWS * (D + 2);              // floats per warp partial
-    static_assert(NCW * WARP_PART * 4 + MAX_ROWS * (D + 2) * 4 <= NST * STAGE, "partials fit in the ring");
+    static_assert(NCW * WARP_PART * 4 + MAX_ROWS * MAX_RG * (D + 2) * 4 <= NST * STAGE, "partials fit in the ring");
 };
 
 // Byte offset of 16-byte chunk `c` (0..15 across boxes) of key row r in a tile.
@@ -184,14 +184,17 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
     const uint32_t bars = smem_u32(smem);
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (NST + s); };
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 8 * 2 * NST);
+    auto rot_bar = [&](int s) { return bars + 8u * (2 * NST + s); };  // RoPE: K tile rotated (row groups > 1)
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 8 * 3 * NST);
     const Abort ab{abort_flag};
     uint8_t* ring = smem + L::OFF_RING;
 
-    const int unit = blockIdx.y / p.NRG, rg = blockIdx.y % p.NRG;
+    const int unit = blockIdx.y;
     const int b = unit / p.Hkv, kvh = unit % p.Hkv;
-    const int row0 = rg * MAX_ROWS;                   // first unit row of this row group
-    const int nrows = min(MAX_ROWS, p.R - row0);      // rows of this row group
+    // consumer warp -> (row group, tile class): tile i goes to the NRG warps of class i % NTG
+    const int NRG = p.NRG, NTG = NCW / NRG;
+    const int wrg = warp % NRG, wtg = warp / NRG;
+    const int row0 = wrg * MAX_ROWS;  // first unit row of this warp's row group
     const uint32_t rank = cluster_rank(), csize = cluster_size();
 
     // visible key range of the unit (union over its rows), split across the cluster
@@ -216,14 +219,15 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         *abort_flag = 0;
         for (int s = 0; s < NST; ++s) {
             mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), 1);
+            mbar_init(empty_bar(s), NRG);  // one arrive per row group's consumer warp
+            mbar_init(rot_bar(s), NRG);
         }
         fence_barrier_init();
     }
     __syncthreads();
 
     float* part = reinterpret_cast<float*>(ring);                 // [NCW][MAX_ROWS][D + 2] after the loop
-    float* cta = part + NCW * L::WARP_PART;                        // [MAX_ROWS][D + 2]: O (D), m, l
+    float* cta = part + NCW * L::WARP_PART;                        // [R][D + 2]: O (D), m, l per unit row
 
     if (warp == NCW) {
         // ------------------------------------------------------------ producer
@@ -299,18 +303,23 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
 
         constexpr int NCH = D / 8;                // 16-byte chunks per key row
         constexpr int RG = NCH < 8 ? NCH : 8;     // chunks per table-load group
-        for (int i = warp; i < ntiles; i += NCW) {
+        for (int i = wtg; i < ntiles; i += NTG) {
             const int s = i % NST, n = i / NST;
             const int k0 = (t_begin + i) * KT;
-            // RoPE: this lane's key row; its first table group loads while the tile is in flight
+            // RoPE: lane = key row; the NRG consumer warps of the tile split its chunks
+            // [c_lo, c_lo + cpw), the first table group loading while the tile is in flight
             const int rkey = k0 + lane;
             const bool rrow = p.rope && rkey < p.KS;  // rows past KS are zero fill
+            const int cpw = NCH / NRG, c_lo = wrg * cpw;
             float4 rc[RG], rs[RG];
             if (rrow) {
 #pragma unroll
                 for (int u = 0; u < RG; ++u) {
-                    rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + static_cast<int64_t>(rkey) * (D / 2) + 4 * u));
-                    rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + static_cast<int64_t>(rkey) * (D / 2) + 4 * u));
+                    if (u < cpw) {
+                        const int64_t ti = static_cast<int64_t>(rkey) * (D / 2) + 4 * (c_lo + u);
+                        rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + ti));
+                        rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + ti));
+                    }
                 }
             }
             bool ok = !aborted && mbar_wait(full_bar(s), n & 1, ab, 0x502);
@@ -326,19 +335,33 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
                 if (rrow) {
 #pragma unroll
                     for (int g0 = 0; g0 < NCH; g0 += RG) {
+                        if (g0 >= cpw) break;
                         if (g0 > 0) {
 #pragma unroll
                             for (int u = 0; u < RG; ++u) {
-                                const int64_t ti = static_cast<int64_t>(rkey) * (D / 2) + 4 * (g0 + u);
-                                rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + ti));
-                                rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + ti));
+                                if (g0 + u < cpw) {
+                                    const int64_t ti = static_cast<int64_t>(rkey) * (D / 2) + 4 * (c_lo + g0 + u);
+                                    rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + ti));
+                                    rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + ti));
+                                }
                             }
                         }
 #pragma unroll
-                        for (int u = 0; u < RG; ++u) rotate_chunk(ktile + tile_off<D>(lane, g0 + u), rc[u], rs[u]);
+                        for (int u = 0; u < RG; ++u)
+                            if (g0 + u < cpw) rotate_chunk(ktile + tile_off<D>(lane, c_lo + g0 + u), rc[u], rs[u]);
                     }
                 }
                 __syncwarp();  // every row rotated before ldmatrix reads across rows
+                if (NRG > 1) {
+                    // the other row groups' warps rotated the rest of the tile
+                    if (lane == 0) mbar_arrive(rot_bar(s));
+                    bool rok = mbar_wait(rot_bar(s), n & 1, ab, 0x503);
+                    rok = __all_sync(0xffffffffu, rok);
+                    if (!rok) {
+                        aborted = true;
+                        continue;
+                    }
+                }
             }
 
             // S = Q K^T over 32 keys: 4 n-tiles of 8 keys
@@ -451,21 +474,23 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         }
         named_bar_sync(1, 32 * NCW);
         // combine the 4 warp partials into the CTA partial
-        for (int idx = threadIdx.x; idx < nrows * D; idx += 32 * NCW) {
-            const int r = idx / D, d = idx % D;
+        // combine, per unit row, the partials of the warps of its row group
+        for (int idx = threadIdx.x; idx < p.R * D; idx += 32 * NCW) {
+            const int ur = idx / D, d = idx % D;
+            const int rgu = ur / MAX_ROWS, r = ur % MAX_ROWS;
             float M = -INFINITY;
-            for (int w = 0; w < NCW; ++w) M = fmaxf(M, part[w * L::WARP_PART + r * (D + 2) + D]);
+            for (int k = 0; k < NTG; ++k) M = fmaxf(M, part[(rgu + k * NRG) * L::WARP_PART + r * (D + 2) + D]);
             float o = 0.f, l = 0.f;
-            for (int w = 0; w < NCW; ++w) {
-                const float* q = part + w * L::WARP_PART + r * (D + 2);
+            for (int k = 0; k < NTG; ++k) {
+                const float* q = part + (rgu + k * NRG) * L::WARP_PART + r * (D + 2);
                 const float f = (M == -INFINITY) ? 0.f : ex2(q[D] - M);
                 o += q[d] * f;
                 l += q[D + 1] * f;
             }
-            cta[r * (D + 2) + d] = o;
+            cta[ur * (D + 2) + d] = o;
             if (d == 0) {
-                cta[r * (D + 2) + D] = M;
-                cta[r * (D + 2) + D + 1] = l;
+                cta[ur * (D + 2) + D] = M;
+                cta[ur * (D + 2) + D + 1] = l;
             }
         }
     }
@@ -474,7 +499,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
     cluster_sync_all();
     if (rank == 0 && warp < NCW) {
         const uint32_t cta_base = smem_u32(cta);
-        for (int idx = threadIdx.x; idx < nrows * (D / 8); idx += 32 * NCW) {
+        for (int idx = threadIdx.x; idx < p.R * (D / 8); idx += 32 * NCW) {
             const int r = idx / (D / 8), c8 = idx % (D / 8);
             float M = -INFINITY;
             for (uint32_t cr = 0; cr < csize; ++cr)
@@ -495,8 +520,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
             v.y = pack_half2(o[2] * inv, o[3] * inv);
             v.z = pack_half2(o[4] * inv, o[5] * inv);
             v.w = pack_half2(o[6] * inv, o[7] * inv);
-            const int ur = row0 + r;  // unit row
-            const int h = kvh * p.G + ur / p.S, s = ur % p.S;
+            const int h = kvh * p.G + r / p.S, s = r % p.S;
             if (!*abort_flag)
                 *reinterpret_cast<uint4*>(p.o + b * p.osb + h * p.osh + s * p.oss + 8 * c8) = v;
         }

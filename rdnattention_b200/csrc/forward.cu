@@ -368,10 +368,10 @@ int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
         (e = make_map(&tmV, vv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 64, KT, CU_TENSOR_MAP_SWIZZLE_128B)))
         return fail(err, "%s", e);
 
-    p.NRG = (p.R + MAX_ROWS - 1) / MAX_ROWS;
-    // one cluster per (unit, row group); a unit's row groups are adjacent in y
-    const int64_t units = static_cast<int64_t>(p.B) * p.Hkv * p.NRG;
-    if (units > 65535) return fail(err, "too many (batch, kv head, row group) units for one decode launch");
+    // row groups of 16 rows inside the CTA; their count divides the consumer warps
+    p.NRG = p.R <= MAX_ROWS ? 1 : p.R <= 2 * MAX_ROWS ? 2 : 4;
+    const int64_t units = static_cast<int64_t>(p.B) * p.Hkv;
+    if (units > 65535) return fail(err, "too many (batch, kv head) units for one decode launch");
     const int64_t tiles = (static_cast<int64_t>(p.KS) + KT - 1) / KT;
     // Cluster size: the smallest split (fewest CTAs, least combine work) whose
     // waves over the SMs (one CTA each) are >= 95% full; each CTA keeps >= 8 tiles.
