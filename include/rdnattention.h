@@ -84,10 +84,13 @@ RDNA_API int32_t rdna_attention_forward_int8qk(
 /* ---- Extensions beyond the reference ABI (no counterpart there) ---- */
 
 /* Bytes of device workspace rdna_attention_forward_ws() needs for this
- * problem: 0 without RoPE; with RoPE, room for the rotated Q and K (fp16),
- * which a pre-pass writes once per call so the attention tiles arrive
- * rotated.  (rdna_attention_forward itself obtains that workspace with
- * cudaMallocAsync/cudaFreeAsync on `stream`.) */
+ * problem: 0 without RoPE; with RoPE, room for the rotated K (fp16), which a
+ * pre-pass writes once per call so the attention kernel's K tiles arrive
+ * rotated, plus the rotated Q for head_dim > 128 (head_dim <= 128 kernels
+ * rotate Q themselves).  Each part is rounded up to 256 bytes.  0 for
+ * decode-shaped problems (seq_len x GQA group <= 64, head_dim 64 or 128),
+ * whose kernel rotates in place.  (rdna_attention_forward itself obtains the
+ * workspace with cudaMallocAsync/cudaFreeAsync on `stream`.) */
 RDNA_API uint64_t rdna_attention_forward_workspace_size(
     uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
     uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim, int32_t has_rope);
@@ -119,12 +122,12 @@ RDNA_API int32_t rdna_attention_forward_ws(
  * is unavailable).  Same arguments and return codes as
  * rdna_attention_forward.
  *
- * The RoPE workspace (rotated Q and K, fp16, each rounded up to 256 bytes)
- * lives in a fixed 32 MiB array inside the library, which every GPU that
- * loads the library keeps reserved until the process exits; a problem whose
- * workspace exceeds it (for example batch 1, 32 heads / 8 KV heads, 2048
- * tokens, head_dim 128 fits; 4096 tokens does not) returns -3 with a message
- * naming the limit.  Without RoPE no workspace is used.  The first call on a
+ * The RoPE workspace (rdna_attention_forward_workspace_size bytes) lives in
+ * a fixed 32 MiB array inside the library, which every GPU that loads the
+ * library keeps reserved until the process exits; a problem whose workspace
+ * exceeds it (for example 8 KV heads, head_dim 128: up to 16384 keys in
+ * total over the batch fit, 20480 do not) returns -3 with a message naming
+ * the limit.  Without RoPE no workspace is used.  The first call on a
  * device looks up the array's device address on that device; make that
  * first call before any stream capture.  All calls share the one array:
  * calls that overlap on the GPU (different streams or threads) race on it,

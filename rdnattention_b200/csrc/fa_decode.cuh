@@ -39,6 +39,7 @@
 #include <math.h>
 
 #include "rdna/forward.hpp"
+#include "rope.cuh"
 #include "sm100.cuh"
 
 namespace rdna {
@@ -73,24 +74,6 @@ struct Params {
     const float* rope_cos;
     const float* rope_sin;
 };
-
-// (x[2i], x[2i+1]) -> (a*c - b*s, a*s + b*c), fp32, rounded to fp16
-__device__ __forceinline__ uint32_t rotate_pair(uint32_t v, float c, float s) {
-    const __half2 h2 = *reinterpret_cast<const __half2*>(&v);
-    const float a = __low2float(h2), b = __high2float(h2);
-    const __half2 r = __floats2half2_rn(a * c - b * s, a * s + b * c);
-    return *reinterpret_cast<const uint32_t*>(&r);
-}
-
-// One 16-byte chunk (4 pairs) of a key row, in place.
-__device__ __forceinline__ void rotate_chunk(uint8_t* ptr, const float4& c, const float4& s) {
-    uint4 x = *reinterpret_cast<const uint4*>(ptr);
-    x.x = rotate_pair(x.x, c.x, s.x);
-    x.y = rotate_pair(x.y, c.y, s.y);
-    x.z = rotate_pair(x.z, c.z, s.z);
-    x.w = rotate_pair(x.w, c.w, s.w);
-    *reinterpret_cast<uint4*>(ptr) = x;
-}
 
 template <int D>
 struct Layout {
@@ -287,7 +270,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
                     v = *reinterpret_cast<const uint32_t*>(p.q + b * p.qsb + h * p.qsh + s * p.qss + dc);
                     if (p.rope) {
                         const int64_t ti = static_cast<int64_t>(s) * (D / 2) + dc / 2;
-                        v = rotate_pair(v, __ldg(p.rope_cos + ti), __ldg(p.rope_sin + ti));
+                        v = rope::rotate_pair(v, __ldg(p.rope_cos + ti), __ldg(p.rope_sin + ti));
                     }
                 }
                 qa[kk][j] = v;
@@ -348,7 +331,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
                         }
 #pragma unroll
                         for (int u = 0; u < RG; ++u)
-                            if (g0 + u < cpw) rotate_chunk(ktile + tile_off<D>(lane, c_lo + g0 + u), rc[u], rs[u]);
+                            if (g0 + u < cpw) rope::rotate_chunk(ktile + tile_off<D>(lane, c_lo + g0 + u), rc[u], rs[u]);
                     }
                 }
                 __syncwarp();  // every row rotated before ldmatrix reads across rows

@@ -55,6 +55,7 @@
 #include <cuda_fp16.h>
 #include <math.h>
 
+#include "rope.cuh"
 #include "sm100.cuh"
 
 namespace rdna {
@@ -85,6 +86,11 @@ struct Params {
     const float* q_vec;
     const float* k_vec;
     const float* v_chan;  // per-channel V scale (B, Hkv, D), or null
+    // RoPE applied to Q inside the kernel (T::ROPE_Q kernels): Q tiles arrive
+    // unrotated and the softmax warps rotate them in shared memory
+    int rope_q;
+    const float* rope_cos;  // [positions, D/2] fp32
+    const float* rope_sin;
 };
 
 template <int D_, int DVMAX_, int BC_, int NT_, int NSK_, int NSV_, bool I8_, bool SDB_ = false>
@@ -117,6 +123,16 @@ struct Traits {
     // Exp-phase token between the two softmax warpgroups (one warpgroup on the
     // MUFU at a time).
     static constexpr bool TOKEN = NT == 2 && !PERSIST && RDNA_EXP_TOKEN;
+    // FP16 exponent phase on sm_100's paired fp32 instructions (scale-and-shift
+    // FMAs and row sums two at a time: fewer issues on the softmax critical path)
+#ifndef RDNA_F32X2
+#define RDNA_F32X2 1
+#endif
+    static constexpr bool F32X2 = RDNA_F32X2 != 0;
+    // Kernels that can rotate Q themselves (one item per CTA: the softmax
+    // warps are idle until the first S, so they rotate the Q tile that the
+    // first Q K^T waits for); the RoPE pre-pass then only rotates K.
+    static constexpr bool ROPE_Q = SDB && !PERSIST;
     static_assert(!(SDB && I8), "S double buffering is FP16-only");
     static_assert(NSK <= 8 && NSV <= 8 && (!SDB || NSV >= 2), "ring depth");
     static constexpr int ESZ = I8 ? 1 : 2;
@@ -204,7 +220,8 @@ struct Bars {
     static constexpr int Q_EMPTY = 56;    // Q tiles no longer read (every issuer commits once per item)
     static constexpr int O_EMPTY = 57;    // +NT (O read out of TMEM by the epilogue, one arrive per warp)
     static constexpr int STG_FREE = 59;   // +NT (O store has read the staging buffer)
-    static constexpr int COUNT = 61;
+    static constexpr int Q_ROT = 61;      // Q tiles rotated in place (one arrive per softmax warp)
+    static constexpr int COUNT = 63;
     static constexpr int TMEM_SLOT = COUNT * 8;      // u32 TMEM base
     static constexpr int ABORT_SLOT = COUNT * 8 + 4; // int abort flag
 };
@@ -215,7 +232,7 @@ enum Site : int {
     SITE_MMA_Q = 0x201, SITE_MMA_K = 0x202, SITE_MMA_V = 0x203, SITE_MMA_P = 0x204,
     SITE_SM_S = 0x301, SITE_SM_O = 0x302, SITE_SM_Q = 0x303, SITE_SM_KS = 0x304, SITE_SM_EPI = 0x305,
     SITE_SM_TOKEN = 0x306, SITE_SM_PV = 0x307, SITE_SM_STG = 0x308,
-    SITE_PROD_QEMPTY = 0x103, SITE_MMA_OEMPTY = 0x205,
+    SITE_PROD_QEMPTY = 0x103, SITE_MMA_OEMPTY = 0x205, SITE_MMA_QROT = 0x206, SITE_SM_QROPE = 0x309,
 };
 
 struct Work {
@@ -401,6 +418,58 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const A
     return __all_sync(0xffffffffu, ok);
 }
 
+// RoPE on the item's Q tiles, in place in shared memory (ROPE_Q kernels),
+// by all 4*NT softmax warps together: warp sw takes rows [RPW*sw, RPW*sw+RPW)
+// of every tile as (row, 16-byte chunk) tasks, consecutive lanes on
+// consecutive chunks, so each table load instruction reads whole rows of the
+// cos/sin tables (coalesced) and, when the tiles sit at the same positions
+// (two heads of a GQA group), one table fetch serves both tiles.  The loads
+// are issued before Q_FULL, so their latency overlaps the tiles' TMA; rows
+// past the sequence (TMA zero fill) are left alone.  Ends with a proxy fence:
+// the tensor core reads the rotated tiles through the async proxy.
+template <class T>
+__device__ __forceinline__ bool rotate_q_tiles(const Params& p, const Work& w, uint8_t* smem, int sw, int lane,
+                                               const Abort& ab) {
+    constexpr int NCH = T::D / 8;              // 16-byte chunks (4 pairs) per row
+    constexpr int CPB = T::BOX / 8;            // chunks per box row
+    constexpr int RPW = BM / (4 * T::NT);      // rows per warp
+    constexpr int TPL = RPW * NCH / 32;        // tasks per lane
+    static_assert(RPW * NCH % 32 == 0, "task split");
+    // tile 1 needs its own table rows unless it sits at tile 0's positions
+    const bool own1 = T::NT == 2 && w.valid[1] && !(w.valid[0] && w.row0[0] == w.row0[1]);
+    // table entries for tile 0's positions, and for tile 1's when they differ
+    // (fixed register arrays: no runtime indexing, so nothing goes to local memory)
+    float4 c0[TPL], s0[TPL], c1[TPL], s1[TPL];
+#pragma unroll
+    for (int k = 0; k < TPL; ++k) {
+        const int task = k * 32 + lane;
+        const int row = RPW * sw + task / NCH, ch = task % NCH;
+        const int64_t off = static_cast<int64_t>(row) * (T::D / 2) + ch * 4;
+        if (w.valid[0] && w.row0[0] + row < p.S) {
+            const int64_t o = static_cast<int64_t>(w.row0[0]) * (T::D / 2) + off;
+            c0[k] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + o));
+            s0[k] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + o));
+        }
+        if (own1 && w.row0[1] + row < p.S) {
+            const int64_t o = static_cast<int64_t>(w.row0[1]) * (T::D / 2) + off;
+            c1[k] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + o));
+            s1[k] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + o));
+        }
+    }
+    if (!warp_wait(smem_u32(smem) + 8u * Bars::Q_FULL, 0, ab, SITE_SM_QROPE)) return false;
+#pragma unroll
+    for (int k = 0; k < TPL; ++k) {
+        const int task = k * 32 + lane;
+        const int row = RPW * sw + task / NCH, ch = task % NCH;
+        const uint32_t off = (ch / CPB) * T::Q_BOX_BYTES + swz_off<T::SW>(row, ch % CPB);
+        if (w.valid[0] && w.row0[0] + row < p.S) rope::rotate_chunk(smem + T::OFF_Q + off, c0[k], s0[k]);
+        if (T::NT == 2 && w.valid[1] && w.row0[1] + row < p.S)
+            rope::rotate_chunk(smem + T::OFF_Q + T::Q_TILE + off, own1 ? c1[k] : c0[k], own1 ? s1[k] : s0[k]);
+    }
+    fence_proxy_async_smem();
+    return true;
+}
+
 // Softmax warpgroup for tile t.  Loops never exit early and no named
 // barriers are used: after an abort every remaining wait returns false at
 // once and the work is skipped, so all threads reach the kernel's final
@@ -432,6 +501,14 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
     const Item I = make_item<T>(p, item);
     const Work& w = I.w;
     const int dv = I.dv, dv0 = I.dv0;
+    if constexpr (T::ROPE_Q) {
+        if (p.rope_q) {
+            // every softmax warp rotates its rows of all tiles (one item per CTA: Q_FULL phase 0)
+            if (!rotate_q_tiles<T>(p, w, smem, warp, lane, ab)) aborted = true;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(Bars::Q_ROT));
+        }
+    }
     if (!w.valid[t]) continue;  // uniform for the warpgroup (no O store, no phases used)
     const int row0 = w.row0[t];
     const int q = row0 + r;
@@ -621,7 +698,29 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         // one chunk of packed P is live at a time.  8 independent partial sums keep
         // the row-sum dependency chain short.
         float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if constexpr (!T::I8) {
+        if constexpr (!T::I8 && T::F32X2) {
+            const float mul = (sl2 > 0.f) ? sl2 : 1.f;
+            const uint64_t mul2 = f2(mul, mul), nm2 = f2(neg_m, neg_m);
+            uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};  // (0.f, 0.f)
+            // all exponentials on the MUFU: moving a share to the FMA pipe
+            // (polynomial exp2) measured slower, the MUFU is not the limit here
+#pragma unroll
+            for (int c0 = 0; c0 < T::BC; c0 += 32) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int c = 0; c < 32; c += 2) {
+                    float a0, a1;
+                    f2_split(ffma2(f2(x[c0 + c], x[c0 + c + 1]), mul2, nm2), a0, a1);
+                    const float p0 = ex2(a0);
+                    const float p1 = ex2(a1);
+                    ls2[(c >> 1) & 3] = fadd2(ls2[(c >> 1) & 3], f2(p0, p1));
+                    pk[c / 2] = pack_half2(p0, p1);
+                }
+                tmem_st_x16(tS + c0 / 2, pk);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) f2_split(ls2[i], ls[2 * i], ls[2 * i + 1]);
+        } else if constexpr (!T::I8) {
             const float mul = (sl2 > 0.f) ? sl2 : 1.f;
 #pragma unroll
             for (int c0 = 0; c0 < T::BC; c0 += 32) {
@@ -630,8 +729,6 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
                 for (int c = 0; c < 32; c += 2) {
                     const float a0 = fmaf(x[c0 + c], mul, neg_m);
                     const float a1 = fmaf(x[c0 + c + 1], mul, neg_m);
-                    // all exponentials on the MUFU: moving a share to the FMA pipe
-                    // (exp2_fma) measured slower here, the softmax is issue-bound
                     const float p0 = ex2(a0);
                     const float p1 = ex2(a1);
                     ls[(c >> 1) & 7] += p0 + p1;
@@ -937,6 +1034,13 @@ __device__ void mma_role_sdb(const Params& p, uint8_t* smem, uint32_t tmem, cons
             ok = false;
             break;
         }
+        if constexpr (T::ROPE_Q) {
+            // the softmax warps rotate Q in place before the first Q K^T
+            if (p.rope_q && !mbar_wait(bar(Bars::Q_ROT), n & 1, ab, SITE_MMA_QROT)) {
+                ok = false;
+                break;
+            }
+        }
         tc_fence_after();
         for (int jj = jlo; jj < jhi && jj < jlo + 2; ++jj) {
             const int ks = kc % T::NSK;
@@ -1148,6 +1252,7 @@ __global__ void __launch_bounds__(T::THREADS, 1)
             mbar_init(bar(Bars::EXPD + t), 4);
         }
         mbar_init(bar(Bars::Q_EMPTY), T::NI);
+        mbar_init(bar(Bars::Q_ROT), 4 * T::NT);
         for (int t = 0; t < T::NT; ++t) {
             mbar_init(bar(Bars::O_EMPTY + t), 4);
             mbar_init(bar(Bars::STG_FREE + t), 1);

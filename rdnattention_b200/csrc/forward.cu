@@ -126,6 +126,7 @@ const char* check_common(const Common& c) {
 template <class T>
 int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t stream, CUtensorMapDataType dt) {
     using namespace prefill;
+    if (p.rope_q && !T::ROPE_Q) return fail(err, "internal: Q rotation requested from a kernel without it");
     CUtensorMap tmQ, tmK, tmV, tmO;
     const CUtensorMapSwizzle sw = T::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     const CUtensorMapSwizzle osw = T::O_SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -237,14 +238,21 @@ constexpr size_t kWsAlign = 256;
 
 size_t align_up(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
 
-// Workspace of an FP16 call: rotated Q and K (contiguous fp16) when RoPE is on
-// and the call takes the prefill path (the decode kernel rotates in place).
+// Whether the prefill kernel of this call rotates Q itself (the head_dim <= 128
+// kernels, prefill::Traits::ROPE_Q); otherwise the pre-pass rotates Q too.
+bool q_rope_in_kernel(const ForwardParams& a) {
+    return a.hasRope && a.headDim <= 128 && prefill::Traits<128, 128, 64, 2, 4, 4, false, true>::ROPE_Q;
+}
+
+// Workspace of an FP16 call: rotated K (and Q, see q_rope_in_kernel), contiguous
+// fp16, when RoPE is on and the call takes the prefill path (the decode kernel
+// rotates in place).
 size_t f16_workspace_bytes(const ForwardParams& a) {
     if (!a.hasRope) return 0;
     if (a.numKvHeads != 0 && decode::eligible(a.seqLen, a.numHeads / a.numKvHeads, a.headDim)) return 0;
     const size_t q = static_cast<size_t>(a.batchSize) * a.numHeads * a.seqLen * a.headDim * 2;
     const size_t k = static_cast<size_t>(a.batchSize) * a.numKvHeads * a.keySeqLen * a.headDim * 2;
-    return align_up(q) + align_up(k);
+    return (q_rope_in_kernel(a) ? 0 : align_up(q)) + align_up(k);
 }
 
 int f16_validate(const Common& c, const ForwardParams& a) {
@@ -268,18 +276,20 @@ Common f16_common(const ForwardParams& a) {
                   a.batchSize, a.numHeads, a.numKvHeads, a.seqLen, a.keySeqLen, a.headDim, 2};
 }
 
-// Enqueues the rotation of Q and K into `ws`; rewrites `c` to read the rotated copies.
+// Enqueues the rotation of K (and of Q unless the kernel rotates it) into `ws`;
+// rewrites `c` to read the rotated copies.
 int launch_rope(const ForwardParams& a, Common& c, void* ws, cudaStream_t st) {
     rope::Params rp{};
+    const bool with_q = !q_rope_in_kernel(a);
     __half* qr = static_cast<__half*>(ws);
-    const size_t qbytes = static_cast<size_t>(a.batchSize) * a.numHeads * a.seqLen * a.headDim * 2;
+    const size_t qbytes = with_q ? static_cast<size_t>(a.batchSize) * a.numHeads * a.seqLen * a.headDim * 2 : 0;
     __half* kr = reinterpret_cast<__half*>(static_cast<char*>(ws) + align_up(qbytes));
     rp.t[0] = rope::Tensor4{static_cast<const __half*>(a.q), qr, a.qStrideB, a.qStrideH, a.qStrideS,
                             static_cast<int>(a.batchSize), static_cast<int>(a.numHeads), static_cast<int>(a.seqLen)};
     rp.t[1] = rope::Tensor4{static_cast<const __half*>(a.k), kr, a.kStrideB, a.kStrideH, a.kStrideS,
                             static_cast<int>(a.batchSize), static_cast<int>(a.numKvHeads),
                             static_cast<int>(a.keySeqLen)};
-    const int64_t qrows = static_cast<int64_t>(a.batchSize) * a.numHeads * a.seqLen;
+    const int64_t qrows = with_q ? static_cast<int64_t>(a.batchSize) * a.numHeads * a.seqLen : 0;
     const int64_t krows = static_cast<int64_t>(a.batchSize) * a.numKvHeads * a.keySeqLen;
     if (qrows + krows > INT32_MAX) return fail(g_err_f16, "RoPE pre-pass: too many rows for one launch");
     rp.rows[0] = static_cast<int>(qrows);
@@ -299,10 +309,12 @@ int launch_rope(const ForwardParams& a, Common& c, void* ws, cudaStream_t st) {
     cudaError_t ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
     const int64_t D = a.headDim;
-    c.q = qr;
-    c.qs[0] = static_cast<int64_t>(a.numHeads) * a.seqLen * D;
-    c.qs[1] = static_cast<int64_t>(a.seqLen) * D;
-    c.qs[2] = D;
+    if (with_q) {
+        c.q = qr;
+        c.qs[0] = static_cast<int64_t>(a.numHeads) * a.seqLen * D;
+        c.qs[1] = static_cast<int64_t>(a.seqLen) * D;
+        c.qs[2] = D;
+    }
     c.k = kr;
     c.ks[0] = static_cast<int64_t>(a.numKvHeads) * a.keySeqLen * D;
     c.ks[1] = static_cast<int64_t>(a.keySeqLen) * D;
@@ -315,6 +327,9 @@ int f16_attention(const ForwardParams& a, const Common& c, cudaStream_t st) {
     p.causal = a.causal ? 1 : 0;
     p.window = a.windowSize > 0 ? a.windowSize : 0;
     p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.rope_q = q_rope_in_kernel(a) ? 1 : 0;
+    p.rope_cos = static_cast<const float*>(a.rot_cos);
+    p.rope_sin = static_cast<const float*>(a.rot_sin);
     switch (a.headDim) {
 #define RDNA_D(Dv) \
     case Dv: return dispatch_f16_dim<Dv>(g_err_f16, c, p, st);

@@ -1,6 +1,7 @@
-// RoPE pre-pass: rotates Q and K once per launch into a contiguous fp16
-// workspace, so the attention kernel's tiles are already rotated when TMA
-// brings them into shared memory.
+// RoPE pre-pass: rotates K (and, for the kernels that do not rotate Q
+// themselves, Q) once per launch into a contiguous fp16 workspace, so the
+// attention kernel's K tiles are already rotated when TMA brings them into
+// shared memory.
 //
 // Interleaved pairs, as the reference kernel applies them
 // (src/rdna/fa2_forward_f16.hip:63-77): (x[2i], x[2i+1]) ->
@@ -18,6 +19,27 @@
 
 namespace rdna {
 namespace rope {
+
+// One interleaved pair (x[2i], x[2i+1]) packed as half2 -> (a*c - b*s, a*s + b*c),
+// fp32 math rounded to fp16.  Shared by the pre-pass, the prefill kernel's Q
+// rotation and the decode kernel, so every path rotates identically.
+__device__ __forceinline__ uint32_t rotate_pair(uint32_t v, float c, float s) {
+    const __half2 h2 = *reinterpret_cast<const __half2*>(&v);
+    const float a = __low2float(h2), b = __high2float(h2);
+    // explicit roundings, so every kernel that inlines this computes the same bits
+    const __half2 r = __floats2half2_rn(__fmaf_rn(a, c, -__fmul_rn(b, s)), __fmaf_rn(a, s, __fmul_rn(b, c)));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// One 16-byte chunk (4 pairs) in place; c/s hold the pairs' table entries.
+__device__ __forceinline__ void rotate_chunk(uint8_t* ptr, const float4& c, const float4& s) {
+    uint4 x = *reinterpret_cast<const uint4*>(ptr);
+    x.x = rotate_pair(x.x, c.x, s.x);
+    x.y = rotate_pair(x.y, c.y, s.y);
+    x.z = rotate_pair(x.z, c.z, s.z);
+    x.w = rotate_pair(x.w, c.w, s.w);
+    *reinterpret_cast<uint4*>(ptr) = x;
+}
 
 struct Tensor4 {
     const __half* src;
@@ -55,18 +77,8 @@ __global__ void __launch_bounds__(256) rope_rotate_kernel(const __grid_constant_
         const int64_t toff = static_cast<int64_t>(s) * (p.D / 2) + ch * 4;
         const float4 cv = __ldg(reinterpret_cast<const float4*>(p.cos_t + toff));
         const float4 sv = __ldg(reinterpret_cast<const float4*>(p.sin_t + toff));
-        const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
-        const float ss[4] = {sv.x, sv.y, sv.z, sv.w};
-        const uint32_t* u = reinterpret_cast<const uint32_t*>(&x);
-        uint4 y;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&y);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const __half2 h2 = *reinterpret_cast<const __half2*>(&u[k]);
-            const float a = __low2float(h2), bb = __high2float(h2);
-            const __half2 rr = __floats2half2_rn(a * cc[k] - bb * ss[k], a * ss[k] + bb * cc[k]);
-            w[k] = *reinterpret_cast<const uint32_t*>(&rr);
-        }
+        const uint4 y{rotate_pair(x.x, cv.x, sv.x), rotate_pair(x.y, cv.y, sv.y), rotate_pair(x.z, cv.z, sv.z),
+                      rotate_pair(x.w, cv.w, sv.w)};
         *reinterpret_cast<uint4*>(T.dst + static_cast<int64_t>(r) * p.D + ch * 8) = y;
     }
 }

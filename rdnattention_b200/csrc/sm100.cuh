@@ -280,25 +280,25 @@ RDNA_DEV float fmax3(float a, float b, float c) {
     return r;
 }
 
-// 2^x on the FMA/ALU pipes, for x <= 8 (softmax arguments), leaving the MUFU
-// free for the other exponentials.  Cody-Waite split x = n + f with
-// n = round(x) taken from the low mantissa bits of x + 1.5*2^23, f in
-// [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted for
-// this library (iteratively reweighted least squares for minimax relative
-// error on [-0.5, 0.5]: max relative error 7.5e-5, below fp16's 2^-11); 2^n by
-// adding n to the exponent field.  The polynomial lies in [0.7, 1.42]
-// (exponent field 126 or 127), so clamping x at -126 keeps the biased exponent
-// >= 0: arguments below -126 (masked keys, -inf) give ~1e-38, not a wrapped
-// exponent.
-RDNA_DEV float exp2_fma(float x) {
-    x = fmaxf(x, -126.0f);
-    const float t = x + 12582912.0f;
-    const float n = t - 12582912.0f;
-    const float f = x - n;
-    float p = fmaf(0.0551716685295105f, f, 0.2426111400127411f);
-    p = fmaf(p, f, 0.6932609677314758f);
-    p = fmaf(p, f, 0.9999280571937561f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Two fp32 values in one 64-bit register: operands of sm_100's paired
+// fp32 instructions (fma/add .f32x2, one issue for both lanes).
+RDNA_DEV uint64_t f2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+RDNA_DEV void f2_split(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+RDNA_DEV uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+RDNA_DEV uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
 // Exact int32 -> float for |v| < 2^22 on the ALU/FMA pipes (avoids the

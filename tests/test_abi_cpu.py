@@ -144,13 +144,17 @@ def test_drop_in_import_name():
     assert rdnattention.SUPPORTED_HEAD_DIMS_INT8 == (64, 128)
 
 
-def test_workspace_size_is_the_rotated_q_and_k():
-    """With RoPE the workspace holds the rotated Q and K written by the pre-pass:
-    B*H*S*D*2 and B*Hkv*KS*D*2 bytes, each rounded up to 256; none without RoPE."""
+def test_workspace_size_is_the_rotated_k_and_wide_q():
+    """With RoPE the workspace holds what the pre-pass writes: the rotated K
+    (B*Hkv*KS*D*2 bytes) and, for head_dim > 128 only, the rotated Q
+    (B*H*S*D*2; the head_dim <= 128 kernels rotate Q in shared memory), each
+    rounded up to 256 bytes; none without RoPE."""
     lib = R._lib_handle()
     ws = lib.rdna_attention_forward_workspace_size
-    assert ws(4, 32, 8, 4096, 4096, 128, 1) == 4 * 32 * 4096 * 128 * 2 + 4 * 8 * 4096 * 128 * 2
-    assert ws(1, 3, 1, 5, 7, 32, 1) == 1024 + 512  # 960 and 448 bytes, each rounded up to a multiple of 256
+    assert ws(4, 32, 8, 4096, 4096, 128, 1) == 4 * 8 * 4096 * 128 * 2
+    assert ws(1, 3, 1, 5, 7, 32, 1) == 512  # 448 bytes of K rounded up to a multiple of 256
+    assert ws(1, 4, 2, 100, 100, 256, 1) == 4 * 100 * 256 * 2 + 2 * 100 * 256 * 2
+    assert ws(1, 3, 1, 5, 7, 160, 1) == 4864 + 2304  # 4800 (Q) and 2240 (K) bytes, each rounded up
     assert ws(4, 32, 8, 4096, 4096, 128, 0) == 0
     # decode-shaped problems (seq_len * group <= 64, head_dim 64/128) rotate in place: no workspace
     assert ws(64, 64, 8, 1, 32768, 128, 1) == 0

@@ -80,11 +80,11 @@ def test_noalloc_matches_allocating_entry_point_twice(lib):
 
 
 def test_noalloc_rejects_workspace_beyond_limit(lib):
-    # batch 1, 32 heads / 8 KV heads, 4096 tokens, head_dim 128: 40 MiB of rotated Q + K > 32 MiB
-    B, H, Hkv, S, D = 1, 32, 8, 4096, 128
+    # 8 heads, 128 query rows, 20480 keys, head_dim 128: 40 MiB of rotated K > 32 MiB
+    B, H, Hkv, S, KS, D = 1, 8, 8, 128, 20480, 128
     q = torch.zeros(B, H, S, D, device="cuda", dtype=torch.float16)
-    k = torch.zeros(B, Hkv, S, D, device="cuda", dtype=torch.float16)
-    cos, sin = _tables(S, D, 10000.0)
+    k = torch.zeros(B, Hkv, KS, D, device="cuda", dtype=torch.float16)
+    cos, sin = _tables(KS, D, 10000.0)
     out = torch.empty_like(q)
     rc = _call(lib.rdna_attention_forward_noalloc, q, k, k, out, cos, sin, True, D ** -0.5)
     assert rc == -3
