@@ -303,6 +303,58 @@ def load_peaks():
     return 1590.0, 6650.0, "fallback"
 
 
+# Nominal dense peaks of one B200 (spec sheet), reported beside the measured ones.
+SPEC_PEAKS = {"fp16": 2250.0, "int8": 4500.0, "hbm": 8000.0}
+
+
+def load_int8_peak():
+    """INT8 tensor peak measured on this pool (profiles/int8_peak.txt, written from
+    `python bench.py --measure-int8-peak`), or None."""
+    f = ROOT / "profiles" / "int8_peak.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("int8_tops_burst:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def measure_int8_peak():
+    """torch._int_mm (cuBLASLt int8 x int8 -> int32) at 8192^3: best of 10 single
+    launches (burst) and a 4 s back-to-back loop (sustained), 2 OP per MAC."""
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t().contiguous().t()
+    for _ in range(5):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    ops = 2.0 * n ** 3
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    iters = max(1, int(4000.0 / best))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(torch.cuda.current_device())
+    with sampler:
+        s.record()
+        for _ in range(iters):
+            torch._int_mm(a, b)
+        e.record()
+        torch.cuda.synchronize()
+    sus = s.elapsed_time(e) / iters
+    print(json.dumps({"int8_tops_burst": ops / best / 1e9, "int8_tops_sustained": ops / sus / 1e9,
+                      "iters_sustained": iters, "clocks": sampler.summary(),
+                      "how": "torch._int_mm int8 8192^3 (2*N^3 OP): best of 10 launches; back to back for 4 s"}))
+
+
 def load_traffic(workload):
     """DRAM bytes per launch from a committed ncu summary (profiles/<kernel>_<workload>.txt)."""
     for f in (ROOT / "profiles").glob("*.txt"):
@@ -378,7 +430,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the per-rank batch (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--measure-int8-peak", action="store_true",
+                    help="measure the INT8 tensor peak (torch._int_mm) and exit")
     args = ap.parse_args()
+    if args.measure_int8_peak:
+        measure_int8_peak()
+        return
     cfg = dict(CONFIGS[args.config])
     if args.batch is not None:
         cfg["B"] = args.batch
@@ -444,11 +501,20 @@ def main():
         roof = {"bound": "hbm", "achieved": per_step_units / (ms_step / 1e3) / 1e9, "peak": peak_hbm,
                 "unit": "GB/s"}
     else:
-        peak = peak_tc * (2 if cfg["kind"] == "int8" else 1)
+        peak = peak_tc
+        src = f"{peak_src} (MEASURED_PEAKS.json bf16 burst)"
+        if cfg["kind"] == "int8":
+            i8 = load_int8_peak()
+            peak, src = (i8, "measured (profiles/int8_peak.txt, torch._int_mm burst)") if i8 else \
+                (2 * peak_tc, f"{peak_src} (MEASURED_PEAKS.json bf16 burst x2)")
         roof = {"bound": "tensor", "achieved": per_step_units / (ms_step / 1e3) / 1e12, "peak": peak,
                 "unit": "TOP/s" if cfg["kind"] == "int8" else "TFLOP/s"}
+        peak_src = src
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["peak_source"] = f"{peak_src} (MEASURED_PEAKS.json bf16 burst{' x2 for int8' if cfg['kind']=='int8' else ''})"
+    roof["peak_source"] = peak_src if cfg["kind"] != "decode" else f"{peak_src} (MEASURED_PEAKS.json copy)"
+    spec = SPEC_PEAKS["hbm" if cfg["kind"] == "decode" else cfg["kind"] if cfg["kind"] == "int8" else "fp16"]
+    roof["spec_peak"] = spec
+    roof["frac_of_spec"] = roof["achieved"] / spec
     roof["traffic"] = load_traffic(cfg["workload"])
     roof["algorithmic_bytes"] = algorithmic_bytes(cfg)
 
