@@ -129,6 +129,10 @@ struct Traits {
 #define RDNA_F32X2 1
 #endif
     static constexpr bool F32X2 = RDNA_F32X2 != 0;
+#ifndef RDNA_I8_F32X2
+#define RDNA_I8_F32X2 1
+#endif
+    static constexpr bool I8X2 = I8 && RDNA_I8_F32X2 != 0;  // the same for the INT8 score conversion
     // Kernels that can rotate Q themselves (one item per CTA: the softmax
     // warps are idle until the first S, so they rotate the Q tile that the
     // first Q K^T waits for); the RoPE pre-pass then only rotates K.
@@ -579,7 +583,21 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
             // float(acc) * k_scale; the per-row q_scale * scale * log2(e) (rowscale) is
             // applied to the max and folded into the exponent's FMA below.
             const float* ksb = ksbuf + (gg & 1) * T::BC;
-            if (kvec) {
+            if constexpr (T::I8X2) {
+                // the bias subtraction (exact) and the key-scale product, two at a time
+                const uint64_t mb2 = f2(-12582912.0f, -12582912.0f);
+                if (kvec) {
+#pragma unroll
+                    for (int c = 0; c < T::BC; c += 2) {
+                        const uint64_t v = fadd2(f2(i2f_biased(raw[c]), i2f_biased(raw[c + 1])), mb2);
+                        f2_split(fmul2(v, *reinterpret_cast<const uint64_t*>(ksb + c)), x[c], x[c + 1]);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < T::BC; c += 2)
+                        f2_split(fadd2(f2(i2f_biased(raw[c]), i2f_biased(raw[c + 1])), mb2), x[c], x[c + 1]);
+                }
+            } else if (kvec) {
 #pragma unroll
                 for (int c = 0; c < T::BC; ++c) x[c] = (i2f_biased(raw[c]) - 12582912.0f) * ksb[c];
             } else {
@@ -751,9 +769,19 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
                 uint32_t pk[8];
 #pragma unroll
                 for (int c = 0; c < 32; c += 4) {
-                    const uint32_t e0 = ex2_h2(pack_half2(fmaf(x[c0 + c], ars, neg_m), fmaf(x[c0 + c + 1], ars, neg_m)));
-                    const uint32_t e1 =
-                        ex2_h2(pack_half2(fmaf(x[c0 + c + 2], ars, neg_m), fmaf(x[c0 + c + 3], ars, neg_m)));
+                    float a0, a1, a2, a3;
+                    if constexpr (T::I8X2) {
+                        const uint64_t ars2 = f2(ars, ars), nm2 = f2(neg_m, neg_m);
+                        f2_split(ffma2(f2(x[c0 + c], x[c0 + c + 1]), ars2, nm2), a0, a1);
+                        f2_split(ffma2(f2(x[c0 + c + 2], x[c0 + c + 3]), ars2, nm2), a2, a3);
+                    } else {
+                        a0 = fmaf(x[c0 + c], ars, neg_m);
+                        a1 = fmaf(x[c0 + c + 1], ars, neg_m);
+                        a2 = fmaf(x[c0 + c + 2], ars, neg_m);
+                        a3 = fmaf(x[c0 + c + 3], ars, neg_m);
+                    }
+                    const uint32_t e0 = ex2_h2(pack_half2(a0, a1));
+                    const uint32_t e1 = ex2_h2(pack_half2(a2, a3));
                     hs[(c >> 2) & 7] = hadd2(hs[(c >> 2) & 7], hadd2(e0, e1));
                     pk[c / 4] = pack_half_low_bytes(hfma2(e0, k127, k1024), hfma2(e1, k127, k1024));
                 }

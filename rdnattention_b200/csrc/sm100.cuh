@@ -281,7 +281,7 @@ RDNA_DEV float fmax3(float a, float b, float c) {
 }
 
 // Two fp32 values in one 64-bit register: operands of sm_100's paired
-// fp32 instructions (fma/add .f32x2, one issue for both lanes).
+// fp32 instructions (fma/add/mul .f32x2, one issue for both lanes).
 RDNA_DEV uint64_t f2(float lo, float hi) {
     uint64_t r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
@@ -298,6 +298,11 @@ RDNA_DEV uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
 RDNA_DEV uint64_t fadd2(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+RDNA_DEV uint64_t fmul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
 
