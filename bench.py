@@ -219,36 +219,76 @@ class _Null:
 
 
 def time_e2e(cfg, x, steps, warmup, dist_on):
-    """Public API with host buffers: per step H2D of the inputs from pinned memory,
-    the attention call, D2H of the output; timed with events on the current stream."""
+    """Public API with host buffers, pipelined as a serving loop would run it: every
+    step copies its inputs from pinned host memory to the device (copy stream),
+    calls the attention API on them (compute stream) and copies the output back to
+    pinned host memory (a second copy stream), with two buffer sets so step i+1's
+    upload and step i-1's download overlap step i's attention (the two copy
+    directions use separate copy engines).  Timed from before the first upload to
+    after the last download, with events, max over ranks."""
     import rdnattention_b200 as R
 
-    host = {}
     names = ["qi", "ki", "vi", "qsc", "ksc"] if cfg["kind"] == "int8" else ["q", "k", "v"]
     if cfg["kind"] == "decode":
         names = ["q", "kc", "vc"]
     if cfg["kind"] == "fp16" and "cos" in x:
         names += ["cos", "sin"]
-    for n in names:
-        host[n] = x[n].detach().to("cpu").pin_memory()
-    dev = {n: torch.empty_like(x[n]) for n in names}
-    out_host = torch.empty(x["q"].shape, dtype=torch.float16).pin_memory()
+    host = {n: x[n].detach().to("cpu").pin_memory() for n in names}
+    dev = [{n: torch.empty_like(x[n]) for n in names} for _ in range(2)]
+    out_dev = [torch.empty(x["q"].shape, dtype=torch.float16, device="cuda") for _ in range(2)]
+    out_host = [torch.empty(x["q"].shape, dtype=torch.float16).pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = out_host.numel() * out_host.element_size()
+    d2h = out_host[0].numel() * out_host[0].element_size()
+    s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_done, cmp_done, out_done = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    used = [False, False]
 
-    def once():
-        for n in names:
-            dev[n].copy_(host[n], non_blocking=True)
-        if cfg["kind"] == "int8":
-            o = R.flash_attn_int8qk(dev["qi"], dev["ki"], dev["vi"], dev["qsc"], dev["ksc"], x["vs"])
-        elif cfg["kind"] == "decode":
-            o = R.flash_attn_strided(dev["q"], dev["kc"].transpose(1, 2), dev["vc"].transpose(1, 2))
-        else:
-            o = R.flash_attn(dev["q"], dev["k"], dev["v"], is_causal=cfg["causal"], window_size=cfg["window"],
-                             rot_cos=dev.get("cos"), rot_sin=dev.get("sin"))
-        out_host.copy_(o, non_blocking=True)
+    def step(i):
+        b = i % 2
+        d = dev[b]
+        with torch.cuda.stream(s_in):
+            if used[b]:
+                s_in.wait_event(cmp_done[b])  # step i-2's attention has read these inputs
+            for n in names:
+                d[n].copy_(host[n], non_blocking=True)
+            in_done[b].record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(in_done[b])
+            if used[b]:
+                s_cmp.wait_event(out_done[b])  # step i-2's download has read out_dev[b]
+            o = out_dev[b]
+            if cfg["kind"] == "int8":
+                o.copy_(R.flash_attn_int8qk(d["qi"], d["ki"], d["vi"], d["qsc"], d["ksc"], x["vs"]))
+            elif cfg["kind"] == "decode":
+                R.flash_attn_strided(d["q"], d["kc"].transpose(1, 2), d["vc"].transpose(1, 2), out=o)
+            else:
+                R.flash_attn_strided(d["q"], d["k"], d["v"], is_causal=cfg["causal"], window_size=cfg["window"],
+                                     rot_cos=d.get("cos"), rot_sin=d.get("sin"), out=o)
+            cmp_done[b].record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(cmp_done[b])
+            out_host[b].copy_(out_dev[b], non_blocking=True)
+            out_done[b].record(s_out)
+        used[b] = True
 
-    ms = time_device(once, steps, warmup, dist_on)
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(dist_on)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    for i in range(steps):
+        step(warmup + i)
+    s_in.wait_stream(s_out)
+    end.record(s_in)
+    torch.cuda.synchronize()
+    barrier(dist_on)
+    ms = start.elapsed_time(end)
+    if dist_on:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
     return ms, h2d, d2h
 
 
