@@ -76,6 +76,40 @@ def test_rope_cases(case):
     assert err < 1e-3, f"{name}: rel_rms {err:.3e} (rope.py's expectation is ~4e-4)"
 
 
+# The head_dim <= 128 kernels rotate Q in shared memory (K goes through the
+# pre-pass).  Cases for the rotation's branches: 64-byte-swizzle boxes (D = 32,
+# 96), tile pairs at different positions (odd group sizes: MHA, G = 3) and at
+# the same positions (even G), partial last tiles, key_seq_len != seq_len.
+Q_ROTATION_CASES = [
+    # (B, H, Hkv, S, KS, D, causal)
+    (1, 4, 4, 200, 200, 32, True),
+    (2, 6, 2, 333, 333, 32, False),
+    (1, 4, 4, 257, 257, 96, True),
+    (1, 8, 2, 300, 300, 96, False),
+    (2, 6, 2, 129, 400, 64, False),
+    (1, 3, 1, 384, 384, 128, True),
+    (1, 8, 2, 70, 600, 128, False),
+    (1, 8, 4, 520, 260, 128, False),
+]
+
+
+@pytest.mark.parametrize("case", Q_ROTATION_CASES, ids=[f"B{c[0]}H{c[1]}/{c[2]}S{c[3]}KS{c[4]}D{c[5]}"
+                                                        f"{'c' if c[6] else ''}" for c in Q_ROTATION_CASES])
+def test_in_kernel_q_rotation(case):
+    B, H, Hkv, S, KS, D, causal = case
+    g = torch.Generator().manual_seed(B * 1000 + S + D)
+    q = torch.randn(B, H, S, D, generator=g).half()
+    k = torch.randn(B, Hkv, KS, D, generator=g).half()
+    v = torch.randn(B, Hkv, KS, D, generator=g).half()
+    cos, sin = rope_tables(max(S, KS), D, 500000.0)
+    got = _run(q, k, v, causal, -1, cos, sin)
+    # the kernel rounds rotated Q and K to fp16, like the reference kernel
+    ref = c_oracle.attention_f16(q, k, v, causal=causal, rot_cos=cos, rot_sin=sin, rope_round=True)
+    diff = (got.double() - ref).abs()
+    assert diff.max().item() <= 2e-3 and diff.mean().item() <= 2e-4, \
+        f"max {diff.max().item():.3e} mean {diff.mean().item():.3e}"
+
+
 @pytest.mark.parametrize("family", ["dense_fp32", "head_dim", "rope", "gate_f16"])
 def test_golden_fixtures(family):
     """Kernel output vs outputs produced by the reference's own oracles."""
