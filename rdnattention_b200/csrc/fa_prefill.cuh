@@ -157,15 +157,19 @@ struct Traits {
     static constexpr int WARP_PROD = 4 * NT;
     static constexpr int WARP_MMA = 4 * NT + 1;
     static constexpr int WARP_QLOAD = 4 * NT + 3;
-    // Register split (NT = 2 only): launched at LAUNCH_REGS per thread.
-    static constexpr bool RESPLIT = NT == 2;
-    static constexpr int LAUNCH_REGS = 168;
+    // One-tile double-buffered kernels run two CTAs per SM (256 TMEM columns,
+    // under half the shared memory each), so one CTA's prologue and epilogue
+    // overlap the other's main loop.
+    static constexpr int MIN_BLOCKS = (NT == 1 && SDB) ? 2 : 1;
+    // Register split: launched at LAUNCH_REGS per thread.
+    static constexpr bool RESPLIT = NT == 2 || MIN_BLOCKS == 2;
+    static constexpr int LAUNCH_REGS = MIN_BLOCKS == 2 ? 128 : 168;
     // 128-key blocks hold 128 scores per softmax thread; 64-key blocks (S
     // double-buffered) need far fewer, and the two MMA issuer warps then keep
     // enough registers not to spill.
-    static constexpr int SOFTMAX_REGS = SDB ? 176 : 216;
-    static constexpr int CONTROL_REGS = SDB ? 152 : 56;
-    static_assert(!RESPLIT || 256 * SOFTMAX_REGS + 128 * CONTROL_REGS <= THREADS * LAUNCH_REGS,
+    static constexpr int SOFTMAX_REGS = MIN_BLOCKS == 2 ? 184 : SDB ? 176 : 216;
+    static constexpr int CONTROL_REGS = MIN_BLOCKS == 2 ? 72 : SDB ? 152 : 56;
+    static_assert(!RESPLIT || 128 * NT * SOFTMAX_REGS + 128 * CONTROL_REGS <= THREADS * LAUNCH_REGS,
                   "register split exceeds the launch allocation");
 
     // TMEM columns
@@ -1242,7 +1246,7 @@ __device__ void mma_role(const Params& p, uint8_t* smem, uint32_t tmem, const Ab
 
 // ---------------------------------------------------------------- kernel
 template <class T>
-__global__ void __launch_bounds__(T::THREADS, 1)
+__global__ void __launch_bounds__(T::THREADS, T::MIN_BLOCKS)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                       const __grid_constant__ Params p) {
