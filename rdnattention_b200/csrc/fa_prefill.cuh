@@ -256,10 +256,21 @@ __device__ __forceinline__ Work decode_work(const Params& p, int item) {
     Work w;
     w.split = item % p.n_split;
     item /= p.n_split;
+    // Causal items differ in length: row blocks slowest, longest rows first
+    // (the block scheduler then balances the tail).  Otherwise every item has
+    // the same length and row blocks vary fastest, so the items that read one
+    // (batch, KV head)'s K/V run in the same wave and find it in L2.
+    const bool rows_fast = p.causal == 0;
     if constexpr (T::NT == 1) {
         const int per = p.B * p.H;
-        const int rb = p.n_rb - 1 - item / per;  // longest causal rows first
-        const int rem = item % per;
+        int rb, rem;
+        if (rows_fast) {
+            rb = item % p.n_rb;
+            rem = item / p.n_rb;
+        } else {
+            rb = p.n_rb - 1 - item / per;
+            rem = item % per;
+        }
         w.b = rem / p.H;
         const int h = rem % p.H;
         w.kvh = h / p.G;
@@ -271,8 +282,14 @@ __device__ __forceinline__ Work decode_work(const Params& p, int item) {
     } else if (p.pair_heads) {
         const int np = p.G / 2;
         const int per = p.B * p.Hkv * np;
-        const int rb = p.n_rb - 1 - item / per;
-        int rem = item % per;
+        int rb, rem;
+        if (rows_fast) {
+            rb = item % p.n_rb;
+            rem = item / p.n_rb;
+        } else {
+            rb = p.n_rb - 1 - item / per;
+            rem = item % per;
+        }
         w.b = rem / (p.Hkv * np);
         rem %= p.Hkv * np;
         w.kvh = rem / np;
@@ -283,8 +300,14 @@ __device__ __forceinline__ Work decode_work(const Params& p, int item) {
         w.valid[0] = w.valid[1] = true;
     } else {
         const int per = p.B * p.H;
-        const int rp = p.n_rp - 1 - item / per;
-        const int rem = item % per;
+        int rp, rem;
+        if (rows_fast) {
+            rp = item % p.n_rp;
+            rem = item / p.n_rp;
+        } else {
+            rp = p.n_rp - 1 - item / per;
+            rem = item % per;
+        }
         w.b = rem / p.H;
         const int h = rem % p.H;
         w.kvh = h / p.G;
