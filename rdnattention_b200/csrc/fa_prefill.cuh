@@ -748,7 +748,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
             const uint64_t mul2 = f2(mul, mul), nm2 = f2(neg_m, neg_m);
             uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};  // (0.f, 0.f)
             // all exponentials on the MUFU: moving a share to the FMA pipe
-            // (polynomial exp2) measured slower, the MUFU is not the limit here
+            // (polynomial exp2) costs about as many issue slots as it saves MUFU time
 #pragma unroll
             for (int c0 = 0; c0 < T::BC; c0 += 32) {
                 uint32_t pk[16];
