@@ -156,7 +156,9 @@ __device__ __forceinline__ void row_range(const Params& p, int s, int& lo, int& 
     }
 }
 
-template <int D>
+// ROPE: compile-time, so the kernel without RoPE keeps the registers the
+// rotation's table values would take.
+template <int D, bool ROPE>
 __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                                                             const __grid_constant__ CUtensorMap tmV,
                                                             const __grid_constant__ Params p) {
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
                     const int r = rows[ri];
                     const int h = kvh * p.G + r / p.S, s = r % p.S;
                     v = *reinterpret_cast<const uint32_t*>(p.q + b * p.qsb + h * p.qsh + s * p.qss + dc);
-                    if (p.rope) {
+                    if constexpr (ROPE) {
                         const int64_t ti = static_cast<int64_t>(s) * (D / 2) + dc / 2;
                         v = rope::rotate_pair(v, __ldg(p.rope_cos + ti), __ldg(p.rope_sin + ti));
                     }
@@ -284,27 +286,33 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         const float sl2 = p.scale_log2;
         bool aborted = false;
 
-        constexpr int NCH = D / 8;                // 16-byte chunks per key row
-        constexpr int RG = NCH < 8 ? NCH : 8;     // chunks per table-load group
+        constexpr int NCH = D / 8;  // 16-byte chunks per key row
+        constexpr int RG = 8;       // RoPE tasks per lane per table-load group
+        // RoPE tasks of a tile: (key row, chunk) pairs, chunk fastest across the
+        // lanes, so 16 (D = 128) or 8 lanes read one whole table row (coalesced);
+        // the tile's NRG consumer warps split the 32 * NCH tasks, tpl per lane
+        const int tpl = KT * NCH / (32 * NRG);
+        const int task0 = wrg * tpl * 32;
         for (int i = wtg; i < ntiles; i += NTG) {
             const int s = i % NST, n = i / NST;
             const int k0 = (t_begin + i) * KT;
-            // RoPE: lane = key row; the NRG consumer warps of the tile split its chunks
-            // [c_lo, c_lo + cpw), the first table group loading while the tile is in flight
-            const int rkey = k0 + lane;
-            const bool rrow = p.rope && rkey < p.KS;  // rows past KS are zero fill
-            const int cpw = NCH / NRG, c_lo = wrg * cpw;
+            // task (g * 32 + lane) of this warp: key row and chunk
+            auto task_row = [&](int g) { return (task0 + g * 32 + lane) / NCH; };
+            auto task_chunk = [&](int g) { return (task0 + g * 32 + lane) % NCH; };
             float4 rc[RG], rs[RG];
-            if (rrow) {
+            auto load_group = [&](int g0) {
 #pragma unroll
                 for (int u = 0; u < RG; ++u) {
-                    if (u < cpw) {
-                        const int64_t ti = static_cast<int64_t>(rkey) * (D / 2) + 4 * (c_lo + u);
+                    const int key = k0 + task_row(g0 + u);
+                    if (g0 + u < tpl && key < p.KS) {  // rows past KS are zero fill
+                        const int64_t ti = static_cast<int64_t>(key) * (D / 2) + 4 * task_chunk(g0 + u);
                         rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + ti));
                         rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + ti));
                     }
                 }
-            }
+            };
+            // the first table group loads while the tile is in flight
+            if constexpr (ROPE) load_group(0);
             bool ok = !aborted && mbar_wait(full_bar(s), n & 1, ab, 0x502);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
@@ -313,25 +321,17 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
             }
             const uint32_t kb = smem_u32(ring + s * L::STAGE);
             const uint32_t vb = kb + L::TILE;
-            if (p.rope) {
+            if constexpr (ROPE) {
                 uint8_t* ktile = ring + s * L::STAGE;
-                if (rrow) {
 #pragma unroll
-                    for (int g0 = 0; g0 < NCH; g0 += RG) {
-                        if (g0 >= cpw) break;
-                        if (g0 > 0) {
+                for (int g0 = 0; g0 < 32 * NCH / 32; g0 += RG) {  // at most tpl <= NCH tasks per lane
+                    if (g0 >= tpl) break;
+                    if (g0 > 0) load_group(g0);
 #pragma unroll
-                            for (int u = 0; u < RG; ++u) {
-                                if (g0 + u < cpw) {
-                                    const int64_t ti = static_cast<int64_t>(rkey) * (D / 2) + 4 * (c_lo + g0 + u);
-                                    rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + ti));
-                                    rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + ti));
-                                }
-                            }
-                        }
-#pragma unroll
-                        for (int u = 0; u < RG; ++u)
-                            if (g0 + u < cpw) rope::rotate_chunk(ktile + tile_off<D>(lane, c_lo + g0 + u), rc[u], rs[u]);
+                    for (int u = 0; u < RG; ++u) {
+                        const int row = task_row(g0 + u);
+                        if (g0 + u < tpl && k0 + row < p.KS)
+                            rope::rotate_chunk(ktile + tile_off<D>(row, task_chunk(g0 + u)), rc[u], rs[u]);
                     }
                 }
                 __syncwarp();  // every row rotated before ldmatrix reads across rows
@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
             }
             // the K rows rewritten by this warp (generic proxy) are ordered before the
             // next TMA write into the slot (async proxy)
-            if (p.rope) fence_proxy_async_smem();
+            if constexpr (ROPE) fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(empty_bar(s));
         }

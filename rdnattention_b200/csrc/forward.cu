@@ -435,18 +435,18 @@ int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    auto launch = [&](auto kern, int smem) {
+        cfg.dynamicSmemBytes = smem;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        return e == cudaSuccess ? cudaLaunchKernelEx(&cfg, kern, tmK, tmV, p) : e;
+    };
     cudaError_t ce;
-    if (D == 64) {
-        cfg.dynamicSmemBytes = Layout<64>::SMEM_BYTES;
-        ce = cudaFuncSetAttribute(fa_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  Layout<64>::SMEM_BYTES);
-        if (ce == cudaSuccess) ce = cudaLaunchKernelEx(&cfg, fa_decode_kernel<64>, tmK, tmV, p);
-    } else {
-        cfg.dynamicSmemBytes = Layout<128>::SMEM_BYTES;
-        ce = cudaFuncSetAttribute(fa_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  Layout<128>::SMEM_BYTES);
-        if (ce == cudaSuccess) ce = cudaLaunchKernelEx(&cfg, fa_decode_kernel<128>, tmK, tmV, p);
-    }
+    if (D == 64)
+        ce = p.rope ? launch(fa_decode_kernel<64, true>, Layout<64>::SMEM_BYTES)
+                    : launch(fa_decode_kernel<64, false>, Layout<64>::SMEM_BYTES);
+    else
+        ce = p.rope ? launch(fa_decode_kernel<128, true>, Layout<128>::SMEM_BYTES)
+                    : launch(fa_decode_kernel<128, false>, Layout<128>::SMEM_BYTES);
     if (ce == cudaSuccess) ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
     return 0;
