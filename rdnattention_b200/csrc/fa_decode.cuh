@@ -28,8 +28,9 @@
 // RoPE (interleaved pairs, reference src/rdna/fa2_forward_f16.hip:63-77, Q
 // row position = its index s within the sequence, K position = key index):
 // Q is rotated as its fragments are loaded; each K tile is rotated in place in
-// shared memory by the warp that consumes it (lane = key row, fp32 math,
-// fp16 result), with the first table loads issued before the tile arrives.
+// shared memory by one of NRW extra rotator warps (warps 5..8, tile i -> warp
+// 5 + i % NRW; fp32 math, fp16 result), whose table loads for the tile are
+// issued while its TMA is in flight; the consumers wait for the rotated tile.
 // The KV cache is read once, as without RoPE; the cos/sin rows come from L2.
 #pragma once
 
@@ -54,7 +55,10 @@ constexpr int NCW = 4;         // consumer warps
 // ever be more than one barrier phase ahead (parity waits cannot alias).
 constexpr int NST = 8;
 static_assert(NST % NCW == 0, "each ring slot needs a single consumer warp");
+constexpr int NRW = 4;         // RoPE rotator warps (RoPE kernels only)
+static_assert(NST % NRW == 0, "each ring slot needs a single rotator warp");
 constexpr int THREADS = 32 * (NCW + 1);
+constexpr int THREADS_ROPE = 32 * (NCW + 1 + NRW);
 constexpr int MAX_ROWS = 16;   // rows per row group (one m16 tile)
 constexpr int MAX_RG = 4;      // row groups per unit: G * seq_len <= 64
 constexpr int MAX_CLUSTER = 8;
@@ -159,7 +163,7 @@ __device__ __forceinline__ void row_range(const Params& p, int s, int& lo, int& 
 // ROPE: compile-time, so the kernel without RoPE keeps the registers the
 // rotation's table values would take.
 template <int D, bool ROPE>
-__global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constant__ CUtensorMap tmK,
+__global__ void __launch_bounds__(ROPE ? THREADS_ROPE : THREADS, 1) fa_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                                                             const __grid_constant__ CUtensorMap tmV,
                                                             const __grid_constant__ Params p) {
     using L = Layout<D>;
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
     const uint32_t bars = smem_u32(smem);
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (NST + s); };
-    auto rot_bar = [&](int s) { return bars + 8u * (2 * NST + s); };  // RoPE: K tile rotated (row groups > 1)
+    auto rot_bar = [&](int s) { return bars + 8u * (2 * NST + s); };  // RoPE: K tile of slot s rotated
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 8 * 3 * NST);
     const Abort ab{abort_flag};
     uint8_t* ring = smem + L::OFF_RING;
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         for (int s = 0; s < NST; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), NRG);  // one arrive per row group's consumer warp
-            mbar_init(rot_bar(s), NRG);
+            mbar_init(rot_bar(s), 1);  // the tile's rotator warp
         }
         fence_barrier_init();
     }
@@ -241,6 +245,54 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
             }
         }
         __syncwarp();  // lanes 1..31 wait here for lane 0's load loop
+    } else if (ROPE && warp > NCW) {
+        // ------------------------------------------------------------ rotators
+        // Tile i -> rotator i % NRW: (key row, 16-byte chunk) tasks, chunk fastest
+        // across the lanes, so 16 (D = 128) or 8 lanes read one whole cos/sin row
+        // per load (coalesced); the first group of table loads is issued while
+        // the tile is in flight.  The proxy fence orders the rotated rows before
+        // the slot's next TMA write.
+        constexpr int NCH = D / 8;   // 16-byte chunks per key row (= tasks per lane)
+        constexpr int RG = 8;        // tasks per table-load group
+        const int rw = warp - NCW - 1;
+        bool aborted = false;
+        for (int i = rw; i < ntiles; i += NRW) {
+            const int s = i % NST, n = i / NST;
+            const int k0 = (t_begin + i) * KT;
+            float4 rc[RG], rs[RG];
+            auto load_group = [&](int g0) {
+#pragma unroll
+                for (int u = 0; u < RG; ++u) {
+                    const int task = (g0 + u) * 32 + lane, key = k0 + task / NCH;
+                    if (g0 + u < NCH && key < p.KS) {  // rows past KS are zero fill
+                        const int64_t ti = static_cast<int64_t>(key) * (D / 2) + 4 * (task % NCH);
+                        rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + ti));
+                        rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + ti));
+                    }
+                }
+            };
+            load_group(0);
+            bool ok = !aborted && mbar_wait(full_bar(s), n & 1, ab, 0x504);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                aborted = true;
+                continue;
+            }
+            uint8_t* ktile = ring + s * L::STAGE;
+#pragma unroll
+            for (int g0 = 0; g0 < NCH; g0 += RG) {
+                if (g0 > 0) load_group(g0);
+#pragma unroll
+                for (int u = 0; u < RG; ++u) {
+                    const int task = (g0 + u) * 32 + lane, row = task / NCH;
+                    if (g0 + u < NCH && k0 + row < p.KS)
+                        rope::rotate_chunk(ktile + tile_off<D>(row, task % NCH), rc[u], rs[u]);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(rot_bar(s));
+        }
     } else {
         // ------------------------------------------------------------ consumers
         const int g = lane >> 2, t = lane & 3;
@@ -286,34 +338,11 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
         const float sl2 = p.scale_log2;
         bool aborted = false;
 
-        constexpr int NCH = D / 8;  // 16-byte chunks per key row
-        constexpr int RG = 8;       // RoPE tasks per lane per table-load group
-        // RoPE tasks of a tile: (key row, chunk) pairs, chunk fastest across the
-        // lanes, so 16 (D = 128) or 8 lanes read one whole table row (coalesced);
-        // the tile's NRG consumer warps split the 32 * NCH tasks, tpl per lane
-        const int tpl = KT * NCH / (32 * NRG);
-        const int task0 = wrg * tpl * 32;
         for (int i = wtg; i < ntiles; i += NTG) {
             const int s = i % NST, n = i / NST;
             const int k0 = (t_begin + i) * KT;
-            // task (g * 32 + lane) of this warp: key row and chunk
-            auto task_row = [&](int g) { return (task0 + g * 32 + lane) / NCH; };
-            auto task_chunk = [&](int g) { return (task0 + g * 32 + lane) % NCH; };
-            float4 rc[RG], rs[RG];
-            auto load_group = [&](int g0) {
-#pragma unroll
-                for (int u = 0; u < RG; ++u) {
-                    const int key = k0 + task_row(g0 + u);
-                    if (g0 + u < tpl && key < p.KS) {  // rows past KS are zero fill
-                        const int64_t ti = static_cast<int64_t>(key) * (D / 2) + 4 * task_chunk(g0 + u);
-                        rc[u] = __ldg(reinterpret_cast<const float4*>(p.rope_cos + ti));
-                        rs[u] = __ldg(reinterpret_cast<const float4*>(p.rope_sin + ti));
-                    }
-                }
-            };
-            // the first table group loads while the tile is in flight
-            if constexpr (ROPE) load_group(0);
-            bool ok = !aborted && mbar_wait(full_bar(s), n & 1, ab, 0x502);
+            // RoPE: the tile's rotator warp signals when K is rotated
+            bool ok = !aborted && mbar_wait(ROPE ? rot_bar(s) : full_bar(s), n & 1, ab, 0x502);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
                 aborted = true;
@@ -321,31 +350,6 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
             }
             const uint32_t kb = smem_u32(ring + s * L::STAGE);
             const uint32_t vb = kb + L::TILE;
-            if constexpr (ROPE) {
-                uint8_t* ktile = ring + s * L::STAGE;
-#pragma unroll
-                for (int g0 = 0; g0 < 32 * NCH / 32; g0 += RG) {  // at most tpl <= NCH tasks per lane
-                    if (g0 >= tpl) break;
-                    if (g0 > 0) load_group(g0);
-#pragma unroll
-                    for (int u = 0; u < RG; ++u) {
-                        const int row = task_row(g0 + u);
-                        if (g0 + u < tpl && k0 + row < p.KS)
-                            rope::rotate_chunk(ktile + tile_off<D>(row, task_chunk(g0 + u)), rc[u], rs[u]);
-                    }
-                }
-                __syncwarp();  // every row rotated before ldmatrix reads across rows
-                if (NRG > 1) {
-                    // the other row groups' warps rotated the rest of the tile
-                    if (lane == 0) mbar_arrive(rot_bar(s));
-                    bool rok = mbar_wait(rot_bar(s), n & 1, ab, 0x503);
-                    rok = __all_sync(0xffffffffu, rok);
-                    if (!rok) {
-                        aborted = true;
-                        continue;
-                    }
-                }
-            }
 
             // S = Q K^T over 32 keys: 4 n-tiles of 8 keys
             float sc[4][4];
@@ -427,9 +431,6 @@ __global__ void __launch_bounds__(THREADS) fa_decode_kernel(const __grid_constan
                     mma16816(oacc[2 * dp + 1], pa[kk2], b2, b3);
                 }
             }
-            // the K rows rewritten by this warp (generic proxy) are ordered before the
-            // next TMA write into the slot (async proxy)
-            if constexpr (ROPE) fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(empty_bar(s));
         }

@@ -426,7 +426,7 @@ int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(cs, static_cast<unsigned>(units), 1);
-    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.blockDim = dim3(p.rope ? THREADS_ROPE : THREADS, 1, 1);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
