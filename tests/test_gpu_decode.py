@@ -96,6 +96,8 @@ def test_decode_full_config5_sampled():
     (1, 16, 1, 1, 3000, 128, False, 512, 1e6),      # MQA, two-sided window
     (1, 4, 4, 1, 33, 128, False, -1, 10000.0),      # key tail (zero-filled rows past KS)
     (2, 16, 2, 3, 1500, 128, True, -1, 500000.0),   # 24 rows per KV head: two row groups
+    (1, 16, 2, 8, 777, 64, False, -1, 10000.0),      # 64 rows per KV head: four row groups, D=64, key tail
+    (1, 8, 1, 5, 1300, 128, True, 256, 1e6),         # 40 rows: four row groups, causal + window
 ])
 def test_decode_rope_vs_oracle(B, H, Hkv, S, KS, D, causal, window, theta):
     """RoPE inside the decode kernel: Q at its row position, each K row at its
