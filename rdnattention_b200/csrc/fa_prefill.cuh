@@ -120,8 +120,9 @@ struct Traits {
 #define RDNA_PERSIST 0
 #endif
     static constexpr bool PERSIST = SDB && RDNA_PERSIST;
-    // Exp-phase token between the two softmax warpgroups (one warpgroup on the
-    // MUFU at a time).
+    // Exp-phase token between the two softmax warpgroups, per scheduler: warp
+    // w of one tile and warp w of the other (the pair that shares a MUFU) take
+    // turns, without waiting for the other schedulers' warps.
     static constexpr bool TOKEN = NT == 2 && !PERSIST && RDNA_EXP_TOKEN;
     // FP16 exponent phase on sm_100's paired fp32 instructions (scale-and-shift
     // FMAs and row sums two at a time: fewer issues on the softmax critical path)
@@ -224,12 +225,12 @@ struct Bars {
     static constexpr int PV_DONE = 46;    // +NT (each PV(t, j) complete; SDB only)
     static constexpr int KS_FULL = 48;    // +2*NT (INT8 per-key scale handoff, by block parity)
     static constexpr int EPI = 52;        // +NT (O staging written)
-    static constexpr int EXPD = 54;       // +NT (softmax exp phase finished, one arrive per warp)
+    static constexpr int EXPD = 63;       // +t*4+q: exp phase of tile t's warp in TMEM lane quadrant q finished
     static constexpr int Q_EMPTY = 56;    // Q tiles no longer read (every issuer commits once per item)
     static constexpr int O_EMPTY = 57;    // +NT (O read out of TMEM by the epilogue, one arrive per warp)
     static constexpr int STG_FREE = 59;   // +NT (O store has read the staging buffer)
     static constexpr int Q_ROT = 61;      // Q tiles rotated in place (one arrive per softmax warp)
-    static constexpr int COUNT = 63;
+    static constexpr int COUNT = 71;
     static constexpr int TMEM_SLOT = COUNT * 8;      // u32 TMEM base
     static constexpr int ABORT_SLOT = COUNT * 8 + 4; // int abort flag
 };
@@ -546,8 +547,9 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
     const int a = I.ta[t], e = I.te[t];
     int klo, khi;
     row_keys(p, q, klo, khi);
-    // Exp-phase order between the two softmax warpgroups: WG0 k, WG1 k, WG0 k+1, ...
-    // (k = each tile's own iteration count), so the MUFU serves one warpgroup at a time.
+    // Exp-phase order between the two warps on this scheduler (warp w of WG0 and
+    // of WG1): WG0 k, WG1 k, WG0 k+1, ... (k = each tile's own iteration count),
+    // so the scheduler's MUFU serves one of them at a time.
     const int other_iters = T::TOKEN ? I.te[1 - t] - I.ta[1 - t] : 0;
 
     float m_ref = -INFINITY;
@@ -734,7 +736,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         if constexpr (T::TOKEN) {
             const int need = it - 1 + t;  // the other warpgroup's exp phase that comes first
             if (need >= 0 && need < other_iters &&
-                !warp_wait(bar(Bars::EXPD + (1 - t)), need & 1, ab, SITE_SM_TOKEN)) {
+                !warp_wait(bar(Bars::EXPD + (1 - t) * 4 + wq), need & 1, ab, SITE_SM_TOKEN)) {
                 aborted = true;
                 continue;
             }
@@ -824,7 +826,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         l += lsum;
         if constexpr (T::TOKEN) {
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(Bars::EXPD + t));
+            if (lane == 0) mbar_arrive(bar(Bars::EXPD + t * 4 + wq));
         }
         tmem_wait_st();
         tc_fence_before();
@@ -1304,7 +1306,7 @@ __global__ void __launch_bounds__(T::THREADS, T::MIN_BLOCKS)
             mbar_init(bar(Bars::KS_FULL + 2 * t), 128);
             mbar_init(bar(Bars::KS_FULL + 2 * t + 1), 128);
             mbar_init(bar(Bars::EPI + t), 128);
-            mbar_init(bar(Bars::EXPD + t), 4);
+            for (int q = 0; q < 4; ++q) mbar_init(bar(Bars::EXPD + t * 4 + q), 1);
         }
         mbar_init(bar(Bars::Q_EMPTY), T::NI);
         mbar_init(bar(Bars::Q_ROT), 4 * T::NT);
