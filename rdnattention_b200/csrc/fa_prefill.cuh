@@ -43,7 +43,7 @@
 //
 // TMEM columns: S(t, b) at [(t*NSB + b)*BC, +BC) (P aliases its first
 // columns); FP16: O_t (fp32) after all S.  INT8: ACC_t (s32 PV accumulator)
-// then O_t (fp32, flushed from ACC whenever the row max moves).
+// then O_t (fp32, folded from ACC whenever the row max moves).
 //
 // Semantics follow the reference kernel (src/rdna/fa2_forward_f16.hip:633-741,
 // src/rdna/fa2_forward_int8qk.hip:229-495): exp2-domain online softmax with
@@ -210,6 +210,11 @@ struct Traits {
 
     static constexpr uint32_t IDESC_QK = instr_desc(I8 ? 2u : 1u, I8 ? 1u : 0u, 0u, BM, BC);
     static constexpr float THRESH = I8 ? 0.0f : 8.0f;  // log2-domain slack before O is rescaled
+    // INT8: the s32 accumulator is folded into O with the exact-below-2^22 conversion
+    // (i2f_biased), so a row folds before its bound on sum(Pq) can pass 2^15 (|V| <= 128
+    // gives |ACC| < 2^22).  One block adds at most 127 * sum(p) + BC/2 <= 128 * BC + BC/2.
+    static constexpr float PQ_FOLD = 32768.f - (128.f * BC + 0.5f * BC);
+    static_assert(!I8 || PQ_FOLD > 0.f, "one block's P keeps the accumulator below 2^22");
 };
 
 // Barrier slots inside the misc region.
@@ -558,7 +563,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
     // INT8 state
     float rowscale = 1.f;
     bool oflushed = false;
-    int since_flush = 0;
+    float pq_acc = 0.f;  // bound on sum(Pq) held in ACC since the last fold
     float* ksbuf = nullptr;
     const bool kvec = T::I8 && p.k_vec != nullptr;
     if constexpr (T::I8) {
@@ -701,33 +706,48 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
                 tmem_wait_st();
             }
         } else {
-            // INT8: the s32 accumulator holds sum(Pq * V) quantised against the current max;
-            // fold it into the fp32 O whenever the max moves (and every 512 blocks, bounding s32).
-            const bool flush = rescale || (it > 0 && since_flush >= 512);
+            // INT8: the s32 accumulator holds sum(Pq * V) quantised against the running
+            // max.  A warp folds it into the fp32 O when any of its rows' max moves, and
+            // before a row's |ACC| can reach 2^22 (the limit of the conversion below):
+            // after this block's PV, ACC holds at most pq_acc + 128 * BC + BC/2 < 2^15
+            // times max|V| <= 128.  Every lane folds (factor 1 where its max did not
+            // move), so the fold has no per-element selects.
+            const bool flush = rescale || (it > 0 && pq_acc >= T::PQ_FOLD);
             if (__any_sync(0xffffffffu, flush)) {
                 const float c = rescale ? corr : 1.f;
-                const float ps = p.pv_scale;
+                const float psc = p.pv_scale * c;
+                const uint64_t psc2 = f2(psc, psc), c2 = f2(c, c), mb2 = f2(-12582912.0f, -12582912.0f);
                 for (int c0 = 0; c0 < dv; c0 += 32) {
                     uint32_t acc[32], o[32];
                     tmem_ld_x32(tACC + c0, acc);
-                    tmem_ld_x32(tO + c0, o);
+                    if (oflushed) {
+                        tmem_ld_x32(tO + c0, o);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float of = oflushed ? __uint_as_float(o[i]) : 0.f;
-                        const float af = i2f_biased(acc[i]) - 12582912.0f;  // |acc| < 2^22 between flushes
-                        o[i] = flush ? __float_as_uint(fmaf(af, ps, of) * c) : o[i];
-                        acc[i] = flush ? 0u : acc[i];
+                        for (int i = 0; i < 32; i += 2) {
+                            const uint64_t af = fadd2(f2(i2f_biased(acc[i]), i2f_biased(acc[i + 1])), mb2);
+                            const uint64_t oc = fmul2(f2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), c2);
+                            float a0, a1;
+                            f2_split(ffma2(af, psc2, oc), a0, a1);
+                            o[i] = __float_as_uint(a0);
+                            o[i + 1] = __float_as_uint(a1);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 2) {
+                            const uint64_t af = fadd2(f2(i2f_biased(acc[i]), i2f_biased(acc[i + 1])), mb2);
+                            float a0, a1;
+                            f2_split(fmul2(af, psc2), a0, a1);
+                            o[i] = __float_as_uint(a0);
+                            o[i + 1] = __float_as_uint(a1);
+                        }
                     }
                     tmem_st_x32(tO + c0, o);
-                    tmem_st_x32(tACC + c0, acc);
+                    tmem_zero_x32(tACC + c0);
                 }
                 tmem_wait_st();
-                if (flush) {
-                    oflushed = true;
-                    since_flush = 0;
-                }
+                oflushed = true;
+                pq_acc = 0.f;
             }
-            ++since_flush;
         }
 
         // P = exp2(s*scale*log2e - m); the row sum uses the unrounded values
@@ -824,6 +844,8 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         }
         lsum = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         l += lsum;
+        // sum(Pq) <= 127 * sum(p) + BC/2; the factor 128 covers the f16 partial sums' rounding
+        if constexpr (T::I8) pq_acc += fmaf(lsum, 128.f, 0.5f * T::BC);
         if constexpr (T::TOKEN) {
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(Bars::EXPD + t * 4 + wq));

@@ -62,6 +62,26 @@ def test_single_block_matches_oracle_closely():
     assert rel_rms(got, ref) < 2e-3
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_flat_prefix_then_max_jump(D):
+    """Flat scores over the first 1024 keys, then a row-max jump of 3 (log2 units)
+    with V at +-127 on every key: the s32 PV accumulator would reach 127*127*1024
+    (about 2^24) before the jump folds it into O.  The kernel folds earlier, while
+    its integer-to-float conversion is exact (|ACC| < 2^22); the oracle differs only
+    by quantising the prefix's p = 1/8 against the global max (16/127 vs 1/8)."""
+    B, H, S, KS = 1, 2, 128, 2048
+    qi = torch.ones(B, H, S, D, dtype=torch.int8)
+    ki = torch.zeros(B, H, KS, D, dtype=torch.int8)
+    ki[:, :, 1024:] = 1
+    sign = torch.where(torch.arange(D) % 3 == 0, -1, 1)
+    vi = (127 * sign).to(torch.int8).expand(B, H, KS, D).contiguous()
+    qs, vs = 0.5, 1.0 / 127.0
+    ks = 3.0 / (np.sqrt(D) * np.log2(np.e) * qs)  # score jump of 3 in the exp2 domain
+    got = R.flash_attn_int8qk(qi.cuda(), ki.cuda(), vi.cuda(), qs, ks, vs).cpu()
+    ref = c_oracle.attention_int8(qi, ki, vi, qs, ks, vs)
+    assert rel_rms(got, ref) < 5e-3
+
+
 def test_baseline_config3_quantized_wrapper():
     """BASELINE config 3 scheme (per-token Q/K, per-channel V) at B=2,H=4,S=2048,D=64,
     vs the fp32 oracle on unquantised inputs (end-to-end accuracy) and vs the INT8
