@@ -101,6 +101,10 @@ size_t noAllocWorkspaceLimit();
 const char* lastError();
 /// Enqueues the INT8 forward on `stream`. Non-blocking. 0 on success.
 int forwardInt8QK(const ForwardParamsInt8QK& params, void* stream);
+/// Debug (extension): forwardInt8QK that also writes the raw int32 Q K^T of every
+/// key block it computes to `scores`, int32 [batch, heads, seq, key_seq]
+/// contiguous (entries of skipped blocks are left as they were).
+int debugInt8QKScores(const ForwardParamsInt8QK& params, void* scores, void* stream);
 /// Reason the most recent forwardInt8QK() / quantizeInt8QKV() call on this thread failed, or nullptr.
 const char* lastErrorInt8QK();
 /// Enqueues the quantisation on `stream`. Non-blocking. 0 on success.

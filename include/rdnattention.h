@@ -182,6 +182,24 @@ RDNA_API int32_t rdna_int8_quantize_qkv(
     void* q_int8, void* k_int8, void* v_int8,
     void* q_scale, void* k_scale, void* v_channel, void* stream);
 
+/* Debug (extension, no counterpart in the reference): rdna_attention_forward_int8qk
+ * that also writes the raw int32 Q K^T of every key block the kernel computes to
+ * `scores`, int32 (batch, num_heads, seq_len, key_seq_len) contiguous; entries of
+ * blocks the masks skip are left untouched.  The tensor cores accumulate int8
+ * products exactly, so these equal the integer dot products.  Other arguments
+ * and return codes as rdna_attention_forward_int8qk. */
+RDNA_API int32_t rdna_debug_int8qk_scores(
+    const void* q, const void* k, const void* v, void* output,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, float q_scale, float k_scale, float v_scale,
+    const void* q_scale_vec, const void* k_scale_vec,
+    int32_t causal, int32_t window_size, void* scores, void* stream);
+
 /* Reads and clears the device status word of the current device: out[0] =
  * first error code a kernel recorded (a bounded wait that expired), out[1] =
  * number of such events.  Synchronises the current device.  Returns 0, or

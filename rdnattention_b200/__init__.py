@@ -74,6 +74,9 @@ def _lib_handle():
         lib.rdna_attention_forward_int8qk_vch.restype = i32
         lib.rdna_int8_quantize_qkv.argtypes = [vp] * 3 + [i64] * 9 + [u32] * 6 + [vp] * 7
         lib.rdna_int8_quantize_qkv.restype = i32
+        lib.rdna_debug_int8qk_scores.argtypes = ([vp] * 4 + [i64] * 12 + [u32] * 6 + [f32] * 4 + [vp, vp]
+                                                 + [i32, i32, vp, vp])
+        lib.rdna_debug_int8qk_scores.restype = i32
         lib.rdna_debug_read_status.argtypes = [ctypes.POINTER(i32)]
         lib.rdna_debug_read_status.restype = i32
         _lib = lib
@@ -255,6 +258,46 @@ def flash_attn_int8qk(query, key, value, q_scale, k_scale, v_scale: float, is_ca
     if rc != 0:
         raise RDNAttentionError(f"flash_attn_int8qk failed: {_last_error()}")
     return out
+
+
+def debug_int8qk_scores(query, key, value, q_scale, k_scale, v_scale: float, is_causal: bool = False,
+                        window_size: int = -1):
+    """flash_attn_int8qk that also returns the kernel's raw int32 Q K^T:
+    (out, scores), scores int32 [batch, heads, seq_len, key_seq_len] with the
+    entries of key blocks the masks skip left at INT32_MIN.  Debug extension
+    (no counterpart in the reference), for checking the integer GEMM bit for bit."""
+    import torch
+
+    _validate_inputs(query, key, value, torch.int8)
+    batch, heads, seq_len, head_dim = query.shape
+    _, kv_heads, key_seq_len, _ = key.shape
+    _check_head_dim(head_dim, "debug_int8qk_scores", allowed=SUPPORTED_HEAD_DIMS_INT8)
+    if not has_device():
+        raise RDNAttentionError("no usable CUDA device found")
+
+    def scale_arg(x, want):
+        if not isinstance(x, torch.Tensor):
+            return float(x), None
+        t = x.to(dtype=torch.float32, device=query.device).contiguous()
+        if tuple(t.shape) != want:
+            raise RDNAttentionError(f"debug_int8qk_scores: scale tensor must be {want}, got {tuple(t.shape)}")
+        return 1.0, t
+
+    q_scalar, q_vec = scale_arg(q_scale, (batch, heads, seq_len))
+    k_scalar, k_vec = scale_arg(k_scale, (batch, kv_heads, key_seq_len))
+    out = torch.empty(query.shape, dtype=torch.float16, device=query.device)
+    scores = torch.full((batch, heads, seq_len, key_seq_len), -2 ** 31, dtype=torch.int32, device=query.device)
+    qs, ks, vs, os_ = query.stride(), key.stride(), value.stride(), out.stride()
+    rc = _lib_handle().rdna_debug_int8qk_scores(
+        query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
+        batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+        float(head_dim ** -0.5), q_scalar, k_scalar, float(v_scale),
+        q_vec.data_ptr() if q_vec is not None else None, k_vec.data_ptr() if k_vec is not None else None,
+        1 if is_causal else 0, int(window_size), scores.data_ptr(), _stream_handle(query.device))
+    if rc != 0:
+        raise RDNAttentionError(f"debug_int8qk_scores failed: {_last_error()}")
+    return out, scores
 
 
 def _symmetric_int8(x, scale):

@@ -182,6 +182,55 @@ RDNA_API int32_t rdna_attention_forward_int8qk(
     return 0;
 }
 
+RDNA_API int32_t rdna_debug_int8qk_scores(
+    const void* q, const void* k, const void* v, void* output,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, float q_scale, float k_scale, float v_scale,
+    const void* q_scale_vec, const void* k_scale_vec,
+    int32_t causal, int32_t window_size, void* scores, void* stream) {
+    rdna::ForwardParamsInt8QK p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = output;
+    p.qStrideB = q_stride_b;
+    p.qStrideH = q_stride_h;
+    p.qStrideS = q_stride_s;
+    p.kStrideB = k_stride_b;
+    p.kStrideH = k_stride_h;
+    p.kStrideS = k_stride_s;
+    p.vStrideB = v_stride_b;
+    p.vStrideH = v_stride_h;
+    p.vStrideS = v_stride_s;
+    p.oStrideB = o_stride_b;
+    p.oStrideH = o_stride_h;
+    p.oStrideS = o_stride_s;
+    p.batchSize = batch_size;
+    p.numHeads = num_heads;
+    p.numKvHeads = num_kv_heads;
+    p.seqLen = seq_len;
+    p.keySeqLen = key_seq_len;
+    p.headDim = head_dim;
+    p.scale = scale;
+    p.qScale = q_scale;
+    p.kScale = k_scale;
+    p.vScale = v_scale;
+    p.causal = causal != 0 ? 1u : 0u;
+    p.windowSize = window_size;
+    p.qScaleVec = q_scale_vec;
+    p.kScaleVec = k_scale_vec;
+    if (rdna::debugInt8QKScores(p, scores, stream) != 0) {
+        set_error("Attention (int8qk) failed: %s", rdna::lastErrorInt8QK());
+        return -3;
+    }
+    return 0;
+}
+
 RDNA_API int32_t rdna_attention_forward_int8qk_vch(
     const void* q, const void* k, const void* v, void* output,
     int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,

@@ -91,9 +91,13 @@ struct Params {
     int rope_q;
     const float* rope_cos;  // [positions, D/2] fp32
     const float* rope_sin;
+    // debug (T::DUMP_S kernels): the raw s32 Q K^T of every computed key block,
+    // int32 [B, H, S, KS] contiguous
+    int32_t* s_dump;
 };
 
-template <int D_, int DVMAX_, int BC_, int NT_, int NSK_, int NSV_, bool I8_, bool SDB_ = false>
+template <int D_, int DVMAX_, int BC_, int NT_, int NSK_, int NSV_, bool I8_, bool SDB_ = false,
+          bool DUMP_S_ = false>
 struct Traits {
     static constexpr int D = D_;          // QK depth (head_dim)
     static constexpr int DVMAX = DVMAX_;  // output columns per CTA (<= 256)
@@ -102,6 +106,9 @@ struct Traits {
     static constexpr int NSK = NSK_;
     static constexpr int NSV = NSV_;
     static constexpr bool I8 = I8_;
+    // debug instantiations (INT8): write the raw s32 Q K^T to Params::s_dump
+    static constexpr bool DUMP_S = DUMP_S_;
+    static_assert(!DUMP_S || I8, "score dump is INT8-only");
     // S double-buffered in TMEM: QK(j+2) is issued right after PV(j), while
     // the softmax works on S(j+1) from the other buffer.
     static constexpr bool SDB = SDB_;
@@ -607,6 +614,14 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
 
         uint32_t raw[T::BC];
         load_s_row<T>(tS, raw);
+        if constexpr (T::DUMP_S) {
+            if (q < p.S) {
+                int32_t* dst = p.s_dump + ((static_cast<int64_t>(w.b) * p.H + w.head[t]) * p.S + q) * p.KS;
+#pragma unroll
+                for (int c = 0; c < T::BC; ++c)
+                    if (j * T::BC + c < p.KS) dst[j * T::BC + c] = static_cast<int32_t>(raw[c]);
+            }
+        }
         float* x = reinterpret_cast<float*>(raw);
         const bool full = block_full<T>(p, row0, j);
         const int lo = klo - j * T::BC, hi = khi - j * T::BC;

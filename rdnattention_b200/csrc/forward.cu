@@ -545,7 +545,8 @@ int forwardF16NoAlloc(const ForwardParams& a, void* stream) {
     return forwardF16Ws(a, ws, kNoAllocWorkspaceBytes, stream);
 }
 
-int forwardInt8QK(const ForwardParamsInt8QK& a, void* stream) {
+namespace {
+int int8_forward(const ForwardParamsInt8QK& a, int32_t* s_dump, void* stream) {
     Common c{a.q, a.k, a.v, a.o,
              {a.qStrideB, a.qStrideH, a.qStrideS}, {a.kStrideB, a.kStrideH, a.kStrideS},
              {a.vStrideB, a.vStrideH, a.vStrideS}, {a.oStrideB, a.oStrideH, a.oStrideS},
@@ -567,11 +568,27 @@ int forwardInt8QK(const ForwardParamsInt8QK& a, void* stream) {
     p.q_vec = static_cast<const float*>(a.qScaleVec);
     p.k_vec = static_cast<const float*>(a.kScaleVec);
     p.v_chan = static_cast<const float*>(a.vChannel);
+    p.s_dump = s_dump;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     constexpr CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    if (s_dump != nullptr) {
+        // debug instantiations: the same kernels plus the score dump
+        if (a.headDim == 64)
+            return launch_prefill<prefill::Traits<64, 64, 128, 2, 4, 4, true, false, true>>(g_err_i8, c, p, st, dt);
+        return launch_prefill<prefill::Traits<128, 128, 128, 1, 3, 3, true, false, true>>(g_err_i8, c, p, st, dt);
+    }
     if (a.headDim == 64)
         return launch_prefill<prefill::Traits<64, 64, 128, 2, 4, 4, true>>(g_err_i8, c, p, st, dt);
     return launch_prefill<prefill::Traits<128, 128, 128, 1, 3, 3, true>>(g_err_i8, c, p, st, dt);
+}
+}  // namespace
+
+int forwardInt8QK(const ForwardParamsInt8QK& a, void* stream) { return int8_forward(a, nullptr, stream); }
+
+int debugInt8QKScores(const ForwardParamsInt8QK& a, void* scores, void* stream) {
+    if (scores == nullptr || (reinterpret_cast<uintptr_t>(scores) & 3u) != 0)
+        return fail(g_err_i8, "scores must be a 4-byte aligned int32 buffer");
+    return int8_forward(a, static_cast<int32_t*>(scores), stream);
 }
 
 int quantizeInt8QKV(const QuantizeInt8Params& a, void* stream) {

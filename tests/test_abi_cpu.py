@@ -91,6 +91,16 @@ def test_int8_argument_errors():
                                              "of numKvHeads")
 
 
+def test_debug_scores_requires_buffer():
+    lib = R._lib_handle()
+    st = (64 * 8 * 64, 8 * 64, 64)
+    rc = lib.rdna_debug_int8qk_scores(16, 16, 16, 16, *st, *st, *st, *st, 1, 8, 8, 64, 64, 64, 0.125, 1.0, 1.0,
+                                      1.0, None, None, 0, -1, None, None)
+    assert rc == -3
+    assert lib.rdna_get_error().decode() == ("Attention (int8qk) failed: scores must be a 4-byte aligned "
+                                             "int32 buffer")
+
+
 def test_error_is_sticky_across_success_and_thread_local():
     rc, msg = _fwd(D=48)
     assert rc == -3

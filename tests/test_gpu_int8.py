@@ -62,6 +62,33 @@ def test_single_block_matches_oracle_closely():
     assert rel_rms(got, ref) < 2e-3
 
 
+@pytest.mark.parametrize("B,H,Hkv,S,KS,D,causal", [
+    (2, 4, 4, 200, 300, 64, False),   # row and key tails, two tiles per CTA
+    (1, 8, 2, 256, 512, 128, False),  # GQA, one tile per CTA
+    (1, 4, 2, 300, 300, 64, True),    # causal: whole skipped blocks are not computed
+])
+def test_int32_scores_bit_exact(B, H, Hkv, S, KS, D, causal):
+    """kind::i8 accumulates exactly: every Q K^T entry the kernel computes equals the
+    integer dot product, over the full int8 range (-128..127), and every visible
+    (row, key) pair is computed."""
+    g = torch.Generator().manual_seed(B * 100 + KS + D)
+    qi = torch.randint(-128, 128, (B, H, S, D), generator=g).to(torch.int8)
+    ki = torch.randint(-128, 128, (B, Hkv, KS, D), generator=g).to(torch.int8)
+    vi = torch.randint(-127, 128, (B, Hkv, KS, D), generator=g).to(torch.int8)
+    _, sc = R.debug_int8qk_scores(qi.cuda(), ki.cuda(), vi.cuda(), 0.01, 0.01, 0.01, is_causal=causal)
+    sc = sc.cpu().long()
+    kx = ki.long().repeat_interleave(H // Hkv, dim=1)
+    ref = torch.einsum("bhqd,bhkd->bhqk", qi.long(), kx)
+    computed = sc != -2 ** 31
+    assert torch.equal(sc[computed], ref[computed])
+    if causal:
+        visible = torch.arange(KS)[None, :] <= torch.arange(S)[:, None] + (KS - S)
+        assert computed[..., visible].all()
+        assert not computed.all()  # blocks past the diagonal were skipped
+    else:
+        assert computed.all()
+
+
 @pytest.mark.parametrize("D", [64, 128])
 def test_flat_prefix_then_max_jump(D):
     """Flat scores over the first 1024 keys, then a row-max jump of 3 (log2 units)
