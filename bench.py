@@ -561,7 +561,9 @@ def main():
         for _ in range(2):
             torch.distributed.all_gather_into_tensor(gathered, o)
         c_ms = time_device(lambda: torch.distributed.all_gather_into_tensor(gathered, o), 5, 0, dist_on)
-        collective = {"op": "nccl all_gather of O", "ms": c_ms / 5, "bytes_per_rank": o.numel() * 2}
+        collective = {"op": "nccl all_gather of O", "ms": c_ms / 5, "bytes_per_rank": o.numel() * 2,
+                      # the same metric with one all-gather added to every step (not overlapped)
+                      "value_incl_collective": per_step_units * world / ((ms_step + c_ms / 5) / 1e3) / scale}
 
     if rank != 0:
         if dist_on:
