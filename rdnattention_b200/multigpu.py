@@ -55,6 +55,20 @@ def local_views(q, k, v, shard: Shard):
     return qs, ks, vs
 
 
+def pieces(shard: Shard, chunks: int):
+    """The shard split into `chunks` consecutive pieces along its own axis (some may
+    be empty), in the order their outputs are all-gathered."""
+    out = []
+    for c in range(chunks):
+        if shard.axis == "batch":
+            lo, hi = _split(shard.b1 - shard.b0, chunks, c)
+            out.append(Shard("batch", shard.b0 + lo, shard.b0 + hi, shard.g0, shard.g1))
+        else:
+            lo, hi = _split(shard.g1 - shard.g0, chunks, c)
+            out.append(Shard("kv_head", shard.b0, shard.b1, shard.g0 + lo, shard.g0 + hi))
+    return out
+
+
 def _default_compute(q, k, v, **kw):
     from . import flash_attn_strided
 
@@ -62,36 +76,58 @@ def _default_compute(q, k, v, **kw):
 
 
 def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: int = -1, rot_cos=None,
-                       rot_sin=None, group=None, compute: Optional[Callable] = None):
+                       rot_sin=None, group=None, compute: Optional[Callable] = None, chunks: int = 1):
     """Forward attention over all ranks of `group`: every rank passes the same full
     [B, H, S, D] / [B, Hkv, KS, D] inputs, computes only its (batch, KV-head) units
     and receives the full output.  `compute` replaces the local kernel call
-    (default: the sm_100a path through the C ABI)."""
+    (default: the sm_100a path through the C ABI).
+
+    chunks > 1 computes each rank's units in that many pieces along its shard axis
+    and starts each piece's all-gather (asynchronous, on the collective's own
+    stream) as soon as the piece is enqueued, so the transfer of piece c overlaps
+    the kernel of piece c + 1.  Every rank takes the same collective steps (pieces
+    that are empty on some ranks are padded)."""
+    if chunks < 1:
+        raise ValueError("chunks must be >= 1")
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     B, H, S, D = query.shape
     Hkv = key.shape[1]
     G = H // Hkv
     compute = compute or _default_compute
-    shards = [plan(B, Hkv, world, r) for r in range(world)]
-    mine = shards[rank]
-    qs, ks, vs = local_views(query, key, value, mine)
+    per_rank = [pieces(plan(B, Hkv, world, r), chunks) for r in range(world)]
 
-    # every rank contributes the same number of elements: pad to the largest shard
-    sizes = [(s.b1 - s.b0) * (s.g1 - s.g0) * G * S * D for s in shards]
-    cap = max(sizes)
-    send = torch.zeros(cap, dtype=query.dtype, device=query.device)
-    if sizes[rank] > 0:
-        o_local = compute(qs, ks, vs, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
-                          rot_sin=rot_sin)
-        send[:sizes[rank]] = o_local.reshape(-1)
-    recv = torch.empty(world * cap, dtype=query.dtype, device=query.device)
-    dist.all_gather_into_tensor(recv, send, group=group)
+    def elems(s: Shard):
+        return (s.b1 - s.b0) * (s.g1 - s.g0) * G * S * D
+
+    gathered = []
+    works = []
+    for c in range(chunks):
+        sizes = [elems(per_rank[r][c]) for r in range(world)]
+        cap = max(sizes)  # every rank contributes the same number of elements
+        if cap == 0:
+            continue
+        send = torch.zeros(cap, dtype=query.dtype, device=query.device) if sizes[rank] < cap else None
+        if sizes[rank] > 0:
+            qs, ks, vs = local_views(query, key, value, per_rank[rank][c])
+            o_local = compute(qs, ks, vs, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
+                              rot_sin=rot_sin).reshape(-1)
+            if send is None:
+                send = o_local
+            else:
+                send[:sizes[rank]] = o_local
+        recv = torch.empty(world * cap, dtype=query.dtype, device=query.device)
+        works.append(dist.all_gather_into_tensor(recv, send, group=group, async_op=True))
+        gathered.append((c, cap, sizes, recv))
+    for w in works:
+        w.wait()
 
     out = torch.empty(B, H, S, D, dtype=query.dtype, device=query.device)
-    for r, s in enumerate(shards):
-        if sizes[r] == 0:
-            continue
-        block = recv[r * cap:r * cap + sizes[r]].view(s.b1 - s.b0, (s.g1 - s.g0) * G, S, D)
-        out[s.b0:s.b1, s.g0 * G:s.g1 * G] = block
+    for c, cap, sizes, recv in gathered:
+        for r in range(world):
+            if sizes[r] == 0:
+                continue
+            s = per_rank[r][c]
+            block = recv[r * cap:r * cap + sizes[r]].view(s.b1 - s.b0, (s.g1 - s.g0) * G, S, D)
+            out[s.b0:s.b1, s.g0 * G:s.g1 * G] = block
     return out

@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from rdnattention_b200.multigpu import flash_attn_sharded, local_views, plan
+from rdnattention_b200.multigpu import flash_attn_sharded, local_views, pieces, plan
 
 
 @pytest.mark.parametrize("B,Hkv,world", [(4, 8, 2), (1, 8, 2), (3, 2, 2), (1, 1, 2), (8, 8, 8), (2, 3, 4), (5, 8, 8)])
@@ -37,7 +37,7 @@ def _free_port():
         return sk.getsockname()[1]
 
 
-def _worker(rank, world, port, shape, causal, window, queue):
+def _worker(rank, world, port, shape, causal, window, queue, chunks=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -52,7 +52,7 @@ def _worker(rank, world, port, shape, causal, window, queue):
         def compute(qs, ks, vs, **kw):
             return torch_oracle.attention(qs, ks, vs, causal=kw["is_causal"], window=kw["window_size"]).half()
 
-        out = flash_attn_sharded(q, k, v, is_causal=causal, window_size=window, compute=compute)
+        out = flash_attn_sharded(q, k, v, is_causal=causal, window_size=window, compute=compute, chunks=chunks)
         ref = torch_oracle.attention(q, k, v, causal=causal, window=window).half()
         queue.put((rank, torch.equal(out, ref)))
     finally:
@@ -66,6 +66,35 @@ def test_sharded_forward_gathers_full_output(shape, causal, window):
     queue = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, shape, causal, window, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert results == {0: True, 1: True}
+
+
+@pytest.mark.parametrize("B,Hkv,world,chunks", [(4, 8, 2, 2), (3, 2, 2, 2), (1, 8, 2, 3), (2, 3, 4, 4), (5, 8, 8, 3)])
+def test_pieces_cover_each_shard_once(B, Hkv, world, chunks):
+    seen = torch.zeros(B, Hkv, dtype=torch.int32)
+    for r in range(world):
+        for p in pieces(plan(B, Hkv, world, r), chunks):
+            seen[p.b0:p.b1, p.g0:p.g1] += 1
+    assert torch.equal(seen, torch.ones_like(seen))
+
+
+@pytest.mark.parametrize("shape,causal,window,chunks", [
+    ((4, 8, 2, 24, 32), True, -1, 2),   # batch axis, even pieces
+    ((3, 4, 1, 9, 32), True, 4, 2),     # batch axis: rank 1's second piece is empty (padded send)
+    ((1, 8, 4, 17, 32), False, 8, 3),   # KV-head axis, uneven pieces
+    ((4, 8, 2, 24, 32), False, -1, 3),  # a piece empty on every rank (skipped by all)
+])
+def test_sharded_forward_overlapped_pieces(shape, causal, window, chunks):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape, causal, window, queue, chunks)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(queue.get(timeout=120) for _ in procs)
