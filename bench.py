@@ -186,34 +186,47 @@ def step_fn(cfg, x):
 
 
 def overlapped_step_fn(cfg, x, world, n_pieces):
-    """One FP16 step that also all-gathers O across the ranks, piece by piece: the
-    rank's batch is split into n_pieces spans, and each span's kernel is followed
-    by an asynchronous NCCL all-gather of its output, which overlaps the next
-    span's kernel (the overlap of rdnattention_b200.multigpu.flash_attn_sharded)."""
+    """One FP16 prefill step that also all-gathers O across the ranks, piece by
+    piece: the rank's units are split into n_pieces spans (of batch elements, or
+    of KV-head groups when the batch is 1, so that every piece of O is
+    contiguous), and each span's kernels are followed by an asynchronous NCCL
+    all-gather of its output, which overlaps the next span's kernels (the
+    overlap of rdnattention_b200.multigpu.flash_attn_sharded).  Returns
+    (fn, axis, pieces)."""
     import rdnattention_b200 as R
 
-    B = cfg["B"]
-    n = max(1, min(n_pieces, B))
-    spans = [(c * B // n, (c + 1) * B // n) for c in range(n)]
+    B, Hkv = cfg["B"], cfg["Hkv"]
+    G = cfg["H"] // Hkv
+    axis = "batch" if B > 1 else "kv_head"
+    units = B if axis == "batch" else Hkv
+    n = max(1, min(n_pieces, units))
+    spans = [(c * units // n, (c + 1) * units // n) for c in range(n)]
     q = x["q"]
     out = torch.empty_like(q)
-    bufs = [torch.empty((world * (b1 - b0),) + tuple(q.shape[1:]), dtype=q.dtype, device=q.device)
-            for b0, b1 in spans]
+
+    def views(a, b):
+        if axis == "batch":
+            return q[a:b], x["k"][a:b], x["v"][a:b], out[a:b]
+        return q[:, a * G:b * G], x["k"][:, a:b], x["v"][:, a:b], out[:, a * G:b * G]
+
+    pieces = [views(a, b) for a, b in spans]
+    bufs = [torch.empty((world * o.numel(),), dtype=o.dtype, device=o.device) for *_, o in pieces]
 
     def fn():
         works = []
-        for (b0, b1), buf in zip(spans, bufs):
-            R.flash_attn_strided(q[b0:b1], x["k"][b0:b1], x["v"][b0:b1], is_causal=cfg["causal"],
-                                 window_size=cfg["window"], rot_cos=x.get("cos"), rot_sin=x.get("sin"),
-                                 out=out[b0:b1])
-            works.append(torch.distributed.all_gather_into_tensor(buf, out[b0:b1], async_op=True))
+        for (qp, kp, vp, op), buf in zip(pieces, bufs):
+            R.flash_attn_strided(qp, kp, vp, is_causal=cfg["causal"], window_size=cfg["window"],
+                                 rot_cos=x.get("cos"), rot_sin=x.get("sin"), out=op)
+            works.append(torch.distributed.all_gather_into_tensor(buf, op.reshape(-1), async_op=True))
         for w in works:
             w.wait()
 
-    return fn
+    fn.out = out  # this rank's O, for checks
+    return fn, axis, n
 
 
 L2_BYTES = 126 * 1024 * 1024
+OVERLAP_PIECES = 2  # pieces of the overlapped all-gather step
 
 
 def input_sets(cfg):
@@ -592,13 +605,13 @@ def main():
         collective = {"op": "nccl all_gather of O", "ms": c_ms / 5, "bytes_per_rank": o.numel() * 2,
                       # the same metric with one all-gather added to every step (not overlapped)
                       "value_incl_collective": per_step_units * world / ((ms_step + c_ms / 5) / 1e3) / scale}
-        if cfg["kind"] != "int8":
-            # the all-gather overlapped with the kernels, piece by piece (same steps on every rank)
-            n_pieces = min(cfg["B"], 4)
+        if cfg["kind"] == "fp16":
+            # prefill: the all-gather overlapped with the kernels, piece by piece (same steps on
+            # every rank); decode's O is small enough that its all-gather needs no overlap
+            ov_fn, ov_axis, ov_n = overlapped_step_fn(cfg, x, world, OVERLAP_PIECES)
             ov_steps = max(3, min(args.steps, 20))
-            ov_ms = time_device(overlapped_step_fn(cfg, x, world, n_pieces), ov_steps, min(args.warmup, 3),
-                                dist_on) / ov_steps
-            collective["overlapped"] = {"pieces": n_pieces, "ms_per_step": ov_ms,
+            ov_ms = time_device(ov_fn, ov_steps, min(args.warmup, 3), dist_on) / ov_steps
+            collective["overlapped"] = {"pieces": ov_n, "axis": ov_axis, "ms_per_step": ov_ms,
                                         "value": per_step_units * world / (ov_ms / 1e3) / scale}
 
     if rank != 0:
