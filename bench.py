@@ -3,19 +3,22 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
 
-Workload (default): BASELINE config 2, the Llama-3-8B-shaped causal GQA
-prefill in FP16 (B=4, Hq=32, Hkv=8, S=4096, D=128, RoPE theta=5e5 applied
-in-kernel).  A step is one rdna_attention_forward call over the whole batch.
-Scaling is weak: every rank owns its own shard of (batch, KV-head group)
-units of the size of the single-GPU workload (global batch = 4 * N); no
-collective runs in the timed region.  `value` is total FLOPs of all ranks
-over the max-over-ranks device time; FLOPs count exactly the visible
-(query, key) pairs, both GEMMs at 2 FLOP/MAC (tests/benchmark.py:77-88).
+Workload (default): the Llama-3-8B-shaped causal GQA prefill in FP16 (B=4,
+Hq=32, Hkv=8, S=4096, D=128, RoPE theta=5e5 applied in-kernel).  On one GPU a
+step is one attention call over the whole batch.  On N GPUs (torchrun) the
+same workload is sharded (strong scaling): each rank computes its rectangle
+of (batch, KV-head group) units (rdnattention_b200.multigpu.plan) and the
+step is the library's flash_attn_sharded call, so the NCCL all-gather that
+assembles the full O on every rank is inside the timed step; the
+compute-only time of the rank's shard is reported beside it.  `value` is the
+workload's FLOPs over the max-over-ranks device time; FLOPs count exactly
+the visible (query, key) pairs, both GEMMs at 2 FLOP/MAC
+(tests/benchmark.py:77-88).
 
-Inputs are synthetic N(0,1) fp16 (seed 0); 335 MB per step stays resident
-in HBM (larger than the 126 MB L2), so no L2 flush is needed between steps.
-Workloads smaller than L2 (configs 1 and 3) rotate through enough
-independent input sets that no step finds its inputs in L2.
+Inputs are synthetic N(0,1) fp16 (seed 0).  A step whose per-rank operands
+are smaller than the 126 MB L2 (the INT8 and small workloads, and the shards
+of the prefill at N >= 4) rotates through enough independent input sets that
+no step finds its inputs in L2; larger ones stay resident, no flush.
 `e2e` times the same call through the public Python API with the step's
 inputs copied in from pinned host memory and the output read back.
 `--impl reference` times the CPU restatement of the reference's algorithm
@@ -185,60 +188,60 @@ def step_fn(cfg, x):
                                         out=out)
 
 
-def overlapped_step_fn(cfg, x, world, n_pieces):
-    """One FP16 prefill step that also all-gathers O across the ranks, piece by
-    piece: the rank's units are split into n_pieces spans (of batch elements, or
-    of KV-head groups when the batch is 1, so that every piece of O is
-    contiguous), and each span's kernels are followed by an asynchronous NCCL
-    all-gather of its output, which overlaps the next span's kernels (the
-    overlap of rdnattention_b200.multigpu.flash_attn_sharded).  Returns
-    (fn, axis, pieces)."""
+def sharded_step_fns(cfg, x, world, rank, chunks):
+    """The N-GPU step on one rank: (full, compute_only, shard).  `full` is the library
+    call a user makes, rdnattention_b200.multigpu.flash_attn_sharded on the full
+    inputs (the rank's units, then the NCCL all-gather that gives every rank the
+    whole O, overlapped piece by piece when chunks > 1); `compute_only` launches
+    the same units' kernel alone."""
     import rdnattention_b200 as R
+    from rdnattention_b200 import multigpu as M
 
-    B, Hkv = cfg["B"], cfg["Hkv"]
-    G = cfg["H"] // Hkv
-    axis = "batch" if B > 1 else "kv_head"
-    units = B if axis == "batch" else Hkv
-    n = max(1, min(n_pieces, units))
-    spans = [(c * units // n, (c + 1) * units // n) for c in range(n)]
-    q = x["q"]
-    out = torch.empty_like(q)
+    kw = {}
+    if cfg["kind"] == "fp16":
+        kw = dict(is_causal=cfg["causal"], window_size=cfg["window"], rot_cos=x.get("cos"), rot_sin=x.get("sin"))
+    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank)
+    qs, ks, vs = M.local_views(x["q"], x["k"], x["v"], shard)
+    out = torch.empty(qs.shape, dtype=torch.float16, device="cuda")
 
-    def views(a, b):
-        if axis == "batch":
-            return q[a:b], x["k"][a:b], x["v"][a:b], out[a:b]
-        return q[:, a * G:b * G], x["k"][:, a:b], x["v"][:, a:b], out[:, a * G:b * G]
+    def full():
+        return M.flash_attn_sharded(x["q"], x["k"], x["v"], chunks=chunks, **kw)
 
-    pieces = [views(a, b) for a, b in spans]
-    bufs = [torch.empty((world * o.numel(),), dtype=o.dtype, device=o.device) for *_, o in pieces]
+    def compute_only():
+        if qs.numel():
+            R.flash_attn_strided(qs, ks, vs, out=out, **kw)
 
-    def fn():
-        works = []
-        for (qp, kp, vp, op), buf in zip(pieces, bufs):
-            R.flash_attn_strided(qp, kp, vp, is_causal=cfg["causal"], window_size=cfg["window"],
-                                 rot_cos=x.get("cos"), rot_sin=x.get("sin"), out=op)
-            works.append(torch.distributed.all_gather_into_tensor(buf, op.reshape(-1), async_op=True))
-        for w in works:
-            w.wait()
-
-    fn.out = out  # this rank's O, for checks
-    return fn, axis, n
+    return full, compute_only, shard
 
 
 L2_BYTES = 126 * 1024 * 1024
-OVERLAP_PIECES = 2  # pieces of the overlapped all-gather step
 
 
-def input_sets(cfg):
-    b = algorithmic_bytes(cfg)
+def input_sets(cfg, world=1):
+    b = rank_bytes(cfg, world)
     return 1 if b >= L2_BYTES else min(256, math.ceil(2 * L2_BYTES / b) + 1)
 
 
-def l2_note(cfg, n_sets):
+def l2_note(cfg, n_sets, world=1):
     if n_sets == 1:
         return "inputs larger than L2, no flush"
-    return (f"{n_sets} rotating input sets ({n_sets * algorithmic_bytes(cfg) / 1e6:.0f} MB > L2): "
+    return (f"{n_sets} rotating input sets ({n_sets * rank_bytes(cfg, world) / 1e6:.0f} MB per rank > L2): "
             "each step's inputs were evicted by the steps before it, no flush")
+
+
+def config_dict(cfg, world, n_sets):
+    """The workload description both arms print (the driver compares them)."""
+    return {"workload": cfg["workload"], "B": cfg["B"], "H": cfg["H"], "Hkv": cfg["Hkv"], "S": cfg["S"],
+            "KS": cfg["KS"], "D": cfg["D"], "causal": cfg["causal"], "window": cfg["window"],
+            "rope_theta": cfg["theta"], "global_batch": cfg["B"],
+            "parallelism": ("one GPU" if world == 1 else
+                            f"(batch, kv-head group) units sharded over {world} ranks + NCCL all-gather of O"),
+            "l2": l2_note(cfg, n_sets, world)}
+
+
+def rank_bytes(cfg, world):
+    """Operand bytes one rank reads and writes per step (its shard of the units)."""
+    return algorithmic_bytes(cfg) / max(1, min(world, cfg["B"] * cfg["Hkv"]))
 
 
 def launches_per_step(cfg):
@@ -357,6 +360,51 @@ def time_e2e(cfg, x, steps, warmup, dist_on):
     return ms, h2d, d2h
 
 
+def time_e2e_sharded(cfg, x, steps, warmup, world, rank):
+    """N GPUs, end to end through the public API with host buffers: every step each
+    rank copies its own units' Q/K/V (and the RoPE tables) in from pinned host
+    memory, computes them, all-gathers O over NCCL (so every rank holds the whole
+    output) and copies its own units' output back to pinned host memory.  Events on
+    the current stream, max over ranks."""
+    import rdnattention_b200 as R
+    from rdnattention_b200 import multigpu as M
+
+    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank)
+    qs, ks, vs = M.local_views(x["q"], x["k"], x["v"], shard)
+    host = {"q": qs.contiguous().cpu().pin_memory(), "k": ks.contiguous().cpu().pin_memory(),
+            "v": vs.contiguous().cpu().pin_memory()}
+    rope = "cos" in x and cfg["kind"] == "fp16"
+    if rope:
+        host["cos"], host["sin"] = x["cos"].cpu().pin_memory(), x["sin"].cpu().pin_memory()
+    dev = {n: torch.empty_like(t, device="cuda") for n, t in host.items()}
+    out_local = torch.empty(host["q"].shape, dtype=torch.float16, device="cuda")
+    out_host = torch.empty(out_local.shape, dtype=torch.float16).pin_memory()
+    G = cfg["H"] // cfg["Hkv"]
+    elems = (shard.b1 - shard.b0) * (shard.g1 - shard.g0) * G * cfg["S"] * cfg["D"]
+    units = [M.plan(cfg["B"], cfg["Hkv"], world, r) for r in range(world)]
+    cap = max((u.b1 - u.b0) * (u.g1 - u.g0) for u in units) * G * cfg["S"] * cfg["D"]
+    send = torch.zeros(cap, dtype=torch.float16, device="cuda")
+    recv = torch.empty(world * cap, dtype=torch.float16, device="cuda")
+    kw = dict(is_causal=cfg["causal"], window_size=cfg["window"]) if cfg["kind"] == "fp16" else {}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def step():
+        for n in host:
+            dev[n].copy_(host[n], non_blocking=True)
+        if qs.numel():
+            R.flash_attn_strided(dev["q"], dev["k"], dev["v"], out=out_local, rot_cos=dev.get("cos"),
+                                 rot_sin=dev.get("sin"), **kw)
+        send[:elems].copy_(out_local.reshape(-1))
+        torch.distributed.all_gather_into_tensor(recv, send)
+        out_host.copy_(out_local, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    ms = time_device(step, steps, 0, True)
+    return ms, h2d, d2h
+
+
 # ---------------------------------------------------------------- CPU baseline
 def cpu_baseline(cfg, max_seconds=10.0):
     """The oracle port (fp32 torch on the host cores) on a bounded sample: whole query
@@ -384,7 +432,7 @@ def cpu_baseline(cfg, max_seconds=10.0):
     while heads < total_heads and (heads == 0 or (time.perf_counter() - t0) < max_seconds):
         h = heads % G
         torch_oracle.attention(q, k, v, causal=cfg["causal"], window=cfg["window"], rot_cos=cos, rot_sin=sin,
-                               heads=range(h, h + 1))
+                               heads=range(h, h + 1), row_chunk=CPU_ROW_CHUNK)
         heads += 1
     secs = time.perf_counter() - t0
     if cfg["kind"] == "decode":
@@ -395,7 +443,8 @@ def cpu_baseline(cfg, max_seconds=10.0):
         done_units = _fl(1, heads, S, KS, D, cfg["causal"], cfg["window"])
         value = done_units / secs / 1e12
     return {"value": value, "unit": metric_of(cfg)[1], "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{heads} query head(s) of {total_heads} (S={S}, KS={KS}, D={D}), fp32 torch oracle, {secs:.1f} s",
+            "sample": f"{heads} query head(s) of {total_heads} (S={S}, KS={KS}, D={D}), fp32 torch oracle "
+                      f"(masked key columns skipped), {secs:.1f} s",
             "host_cpu_count": os.cpu_count()}
 
 
@@ -476,9 +525,11 @@ def load_traffic(workload):
 
 
 # ---------------------------------------------------------------- main
-def run_reference(args, cfg):
-    """CPU arm: the oracle port of the reference algorithm, one query head of the
-    workload per step, on all host threads."""
+def run_reference(args, cfg, world):
+    """CPU arm: the oracle port of the reference algorithm (the reference itself is
+    HIP-only) on the host cores, one query head of the workload per step, masked
+    key columns skipped before the matmul (so the CPU does about the visible-pair
+    work the metric counts)."""
     from oracle import torch_oracle
     from oracle.torch_oracle import flops
 
@@ -497,7 +548,7 @@ def run_reference(args, cfg):
     def one(i):
         h = i % G
         torch_oracle.attention(q, k, v, causal=cfg["causal"], window=cfg["window"], rot_cos=cos, rot_sin=sin,
-                               heads=range(h, h + 1))
+                               heads=range(h, h + 1), row_chunk=CPU_ROW_CHUNK)
 
     for i in range(args.warmup):
         one(i)
@@ -511,16 +562,21 @@ def run_reference(args, cfg):
     else:
         per = flops(1, 1, S, KS, D, cfg["causal"], cfg["window"])
         value = per * args.steps / secs / 1e12
-    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
+    sample = (f"one query head per step ({cfg['H'] * cfg['B']} in the workload), fp32 torch restatement of "
+              "tests/accuracy.py dense_attention_reference + masks + RoPE, masked key columns skipped")
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3 / max(args.steps, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": cfg["workload"], "sample_per_step": "one query head (fp32 torch oracle)"},
+            "config": config_dict(cfg, world, input_sets(cfg, world)),
+            "sample_per_step": "one query head (fp32 torch oracle on the host cores)",
             "cpu_baseline": {"value": value, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": "one query head of batch 0 per step, fp32 torch restatement of "
-                                       "tests/accuracy.py dense_attention_reference + masks + RoPE"},
+                             "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+CPU_ROW_CHUNK = 256  # query rows per CPU matmul: causal chunks skip the keys no row sees
 
 
 def main():
@@ -533,8 +589,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=None, help="override the per-rank batch (profiling runs)")
+    ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--chunks", type=int, default=1,
+                    help="N>1: pieces of the rank's units whose all-gathers overlap the next piece's kernel")
     ap.add_argument("--measure-int8-peak", action="store_true",
                     help="measure the INT8 tensor peak (torch._int_mm) and exit")
     args = ap.parse_args()
@@ -552,7 +610,7 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            run_reference(args, cfg)
+            run_reference(args, cfg, world)
         return
 
     dist_on = world > 1
@@ -565,54 +623,53 @@ def main():
     import rdnattention_b200 as R
 
     R.library_path()  # fail loudly if the CUDA library is missing
-    # Workloads smaller than L2 rotate through enough independent input sets that
-    # each step's data was evicted by the two steps before it (no L2 reuse across
-    # steps without a flush in the timed region).
-    n_sets = input_sets(cfg)
-    xs = [make_inputs(cfg, "cuda", seed=1000 + rank + 7919 * i) for i in range(n_sets)]
+    # Steps whose per-rank operands are smaller than L2 rotate through enough
+    # independent input sets that each step's data was evicted by the two steps
+    # before it (no L2 reuse across steps without a flush in the timed region).
+    # Every rank holds the same full inputs (the sharded call's contract).
+    n_sets = input_sets(cfg, world)
+    xs = [make_inputs(cfg, "cuda", seed=1000 + 7919 * i) for i in range(n_sets)]
     x = xs[0]
-    fns = [step_fn(cfg, xi) for xi in xs]
-    turn = itertools.cycle(fns)
-
-    def fn():
-        next(turn)()
-
     sampler = ClockSampler(local)
-    ms = time_device(fn, args.steps, args.warmup, dist_on, sampler)
-    status = R.debug_read_status()
     per_step_units = work_units(cfg)
-    total_units = per_step_units * world * args.steps
     scale = 1e9 if cfg["kind"] == "decode" else 1e12
-    value = total_units / (ms / 1e3) / scale
+    compute = None
+    if not dist_on:
+        fns = [step_fn(cfg, xi) for xi in xs]
+        turn = itertools.cycle(fns)
+        ms = time_device(lambda: next(turn)(), args.steps, args.warmup, dist_on, sampler)
+        shard = None
+    else:
+        if cfg["kind"] == "int8":
+            raise SystemExit("the sharded INT8 step is not wired into the bench (use --config 2/4a/4b/5)")
+        trip = [sharded_step_fns(cfg, xi, world, rank, args.chunks) for xi in xs]
+        shard = trip[0][2]
+        turn = itertools.cycle([t[0] for t in trip])
+        ms = time_device(lambda: next(turn)(), args.steps, args.warmup, dist_on, sampler)
+        cturn = itertools.cycle([t[1] for t in trip])
+        c_ms = time_device(lambda: next(cturn)(), args.steps, args.warmup, dist_on)
+        units_rank = (shard.b1 - shard.b0) * (shard.g1 - shard.g0)
+        compute = {"what": "the rank's own units alone (no all-gather), max over ranks",
+                   "ms_per_step": c_ms / args.steps,
+                   "value": per_step_units * args.steps / (c_ms / 1e3) / scale,
+                   "units_per_rank_max": None, "units_rank0": units_rank}
+        u = torch.tensor([units_rank], device="cuda", dtype=torch.int64)
+        torch.distributed.all_reduce(u, op=torch.distributed.ReduceOp.MAX)
+        compute["units_per_rank_max"] = int(u.item())
+    status = R.debug_read_status()
+    value = per_step_units * args.steps / (ms / 1e3) / scale
     ms_step = ms / args.steps
 
     e2e = None
     if not args.no_e2e:
         e2e_steps = args.e2e_steps or max(3, min(args.steps, 20))
-        e2e_ms, h2d, d2h = time_e2e(cfg, x, e2e_steps, min(args.warmup, 3), dist_on)
-        e2e_value = per_step_units * world * e2e_steps / (e2e_ms / 1e3) / scale
+        if not dist_on:
+            e2e_ms, h2d, d2h = time_e2e(cfg, x, e2e_steps, min(args.warmup, 3), dist_on)
+        else:
+            e2e_ms, h2d, d2h = time_e2e_sharded(cfg, x, e2e_steps, min(args.warmup, 3), world, rank)
+        e2e_value = per_step_units * e2e_steps / (e2e_ms / 1e3) / scale
         e2e = {"value": e2e_value, "unit": metric_of(cfg)[1], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "steps": e2e_steps}
-
-    # all-gather of O across ranks (result assembly; outside the timed region)
-    collective = None
-    if dist_on:
-        o = torch.empty_like(x["q"])
-        gathered = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=o.device)
-        for _ in range(2):
-            torch.distributed.all_gather_into_tensor(gathered, o)
-        c_ms = time_device(lambda: torch.distributed.all_gather_into_tensor(gathered, o), 5, 0, dist_on)
-        collective = {"op": "nccl all_gather of O", "ms": c_ms / 5, "bytes_per_rank": o.numel() * 2,
-                      # the same metric with one all-gather added to every step (not overlapped)
-                      "value_incl_collective": per_step_units * world / ((ms_step + c_ms / 5) / 1e3) / scale}
-        if cfg["kind"] == "fp16":
-            # prefill: the all-gather overlapped with the kernels, piece by piece (same steps on
-            # every rank); decode's O is small enough that its all-gather needs no overlap
-            ov_fn, ov_axis, ov_n = overlapped_step_fn(cfg, x, world, OVERLAP_PIECES)
-            ov_steps = max(3, min(args.steps, 20))
-            ov_ms = time_device(ov_fn, ov_steps, min(args.warmup, 3), dist_on) / ov_steps
-            collective["overlapped"] = {"pieces": ov_n, "axis": ov_axis, "ms_per_step": ov_ms,
-                                        "value": per_step_units * world / (ov_ms / 1e3) / scale}
 
     if rank != 0:
         if dist_on:
@@ -621,9 +678,11 @@ def main():
 
     metric, unit = metric_of(cfg)
     peak_tc, peak_hbm, peak_src = load_peaks()
+    # the roofline is the per-GPU kernel's: at N > 1 the compute-only time of the rank's units
+    k_ms = compute["ms_per_step"] if compute else ms_step
+    k_units = per_step_units * (compute["units_per_rank_max"] / (cfg["B"] * cfg["Hkv"]) if compute else 1.0)
     if cfg["kind"] == "decode":
-        roof = {"bound": "hbm", "achieved": per_step_units / (ms_step / 1e3) / 1e9, "peak": peak_hbm,
-                "unit": "GB/s"}
+        roof = {"bound": "hbm", "achieved": k_units / (k_ms / 1e3) / 1e9, "peak": peak_hbm, "unit": "GB/s"}
     else:
         peak = peak_tc
         src = f"{peak_src} (MEASURED_PEAKS.json bf16 burst)"
@@ -631,7 +690,7 @@ def main():
             i8 = load_int8_peak()
             peak, src = (i8, "measured (profiles/int8_peak.txt, torch._int_mm burst)") if i8 else \
                 (2 * peak_tc, f"{peak_src} (MEASURED_PEAKS.json bf16 burst x2)")
-        roof = {"bound": "tensor", "achieved": per_step_units / (ms_step / 1e3) / 1e12, "peak": peak,
+        roof = {"bound": "tensor", "achieved": k_units / (k_ms / 1e3) / 1e12, "peak": peak,
                 "unit": "TOP/s" if cfg["kind"] == "int8" else "TFLOP/s"}
         peak_src = src
     roof["frac"] = roof["achieved"] / roof["peak"]
@@ -644,21 +703,19 @@ def main():
 
     line = {
         "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8" if cfg["kind"] == "int8" else "fp16", "data": "synthetic",
-        "config": {"workload": cfg["workload"], "B_per_rank": cfg["B"], "H": cfg["H"], "Hkv": cfg["Hkv"],
-                   "S": cfg["S"], "KS": cfg["KS"], "D": cfg["D"], "causal": cfg["causal"], "window": cfg["window"],
-                   "rope_theta": cfg["theta"], "global_batch": cfg["B"] * world,
-                   "parallelism": f"shard (batch, kv-head group) units x{world}",
-                   "l2": l2_note(cfg, n_sets)},
+        "config": config_dict(cfg, world, n_sets),
         "clocks": sampler.summary(),
         "e2e": e2e,
-        "gpu_launches": args.steps * launches_per_step(cfg),
+        "gpu_launches": args.steps * launches_per_step(cfg) * (args.chunks if dist_on else 1),
         "roofline": roof,
         "kernel_status": list(status),
     }
-    if collective:
-        line["collective"] = collective
+    if compute:
+        line["compute_only"] = compute
+        line["step"] = ("flash_attn_sharded: the rank's units (one kernel per piece), then the NCCL "
+                        f"all-gather of O into every rank ({args.chunks} piece(s))")
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     print(json.dumps(line), flush=True)

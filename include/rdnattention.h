@@ -206,4 +206,15 @@ RDNA_API int32_t rdna_debug_int8qk_scores(
  * -3 with rdna_get_error() set. */
 RDNA_API int32_t rdna_debug_read_status(int32_t* out2);
 
+/* Debug (extension, no counterpart in the reference): a test hook for the
+ * bounded waits.  Until it is called again with withhold_block < 0, prefill
+ * calls made by the calling thread launch with CTA 0 never loading the K tile
+ * of its withhold_block-th key block and with CTA 0's waits limited to
+ * wait_limit_ns: the wait for that tile expires, the CTA records the wait's
+ * site in the status word (rdna_debug_read_status), unwinds (copies in flight
+ * land, issued MMAs drain, TMEM is released) and skips its output store, so
+ * that CTA's rows of O are left unwritten.  Nothing faults or hangs, and the
+ * next call without the hook is unaffected.  Always returns 0. */
+RDNA_API int32_t rdna_debug_set_wait_test(int32_t withhold_block, uint64_t wait_limit_ns);
+
 #endif /* RDNATTENTION_H_ */

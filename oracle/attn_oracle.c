@@ -118,11 +118,22 @@ static void rope_row(float* row, int64_t D, const float* cos_row, const float* s
     }
 }
 
+/*
+ * K rows (rotated when has_rope) and V rows as fp32, prepared once per call
+ * when they fit in memory: kf/vf[(b * Hkv + kvh) * KS + j][D].  The values are
+ * exactly those attend_row_f16 would compute per query row (same conversion,
+ * same rope_row), so the results do not depend on whether the cache is used.
+ */
+typedef struct {
+    float* kf;
+    float* vf;
+} kv_cache_t;
+
 static void attend_row_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* rot_cos,
                            const float* rot_sin, const strides_t* st, int64_t H, int64_t Hkv, int64_t S,
                            int64_t KS, int64_t D, double scale, int causal, int has_rope, int64_t window,
                            int rope_round, int64_t b, int64_t h, int64_t qi, double* out, float* qrow,
-                           float* krow, double* pr) {
+                           float* krow, double* pr, const kv_cache_t* kc) {
     int64_t G = H / Hkv;
     int64_t kvh = h / G;
     const uint16_t* qp = q + b * st->qs_b + h * st->qs_h + qi * st->qs_s;
@@ -136,11 +147,16 @@ static void attend_row_f16(const uint16_t* q, const uint16_t* k, const uint16_t*
 
     double mx = -1e300;
     for (int64_t j = kmin; j <= kmax; j++) {
-        const uint16_t* kp = k + b * st->ks_b + kvh * st->ks_h + j * st->ks_s;
-        for (int64_t d = 0; d < D; d++) krow[d] = h2f(kp[d]);
-        if (has_rope) rope_row(krow, D, rot_cos + j * (D / 2), rot_sin + j * (D / 2), rope_round);
+        const float* kr = krow;
+        if (kc->kf) {
+            kr = kc->kf + ((b * Hkv + kvh) * KS + j) * D;
+        } else {
+            const uint16_t* kp = k + b * st->ks_b + kvh * st->ks_h + j * st->ks_s;
+            for (int64_t d = 0; d < D; d++) krow[d] = h2f(kp[d]);
+            if (has_rope) rope_row(krow, D, rot_cos + j * (D / 2), rot_sin + j * (D / 2), rope_round);
+        }
         double s = 0.0;
-        for (int64_t d = 0; d < D; d++) s += (double)qrow[d] * (double)krow[d];
+        for (int64_t d = 0; d < D; d++) s += (double)qrow[d] * (double)kr[d];
         s *= scale;
         pr[j - kmin] = s;
         if (s > mx) mx = s;
@@ -152,9 +168,14 @@ static void attend_row_f16(const uint16_t* q, const uint16_t* k, const uint16_t*
         sum += p;
     }
     for (int64_t j = kmin; j <= kmax; j++) {
-        const uint16_t* vp = v + b * st->vs_b + kvh * st->vs_h + j * st->vs_s;
         double p = pr[j - kmin];
-        for (int64_t d = 0; d < D; d++) out[d] += p * h2d(vp[d]);
+        if (kc->vf) {
+            const float* vr = kc->vf + ((b * Hkv + kvh) * KS + j) * D;
+            for (int64_t d = 0; d < D; d++) out[d] += p * (double)vr[d];
+        } else {
+            const uint16_t* vp = v + b * st->vs_b + kvh * st->vs_h + j * st->vs_s;
+            for (int64_t d = 0; d < D; d++) out[d] += p * h2d(vp[d]);
+        }
     }
     for (int64_t d = 0; d < D; d++) out[d] /= sum;
 }
@@ -174,6 +195,32 @@ ORACLE_API int oracle_attention_f16(const uint16_t* q, const uint16_t* k, const 
     strides_t st = {qs_b, qs_h, qs_s, ks_b, ks_h, ks_s, vs_b, vs_h, vs_s};
     int64_t total = rows ? nrows : B * H * S;
     int err = 0;
+    /* fp32 K/V cache (up to 1 GiB each) when the call reads each key row many times */
+    kv_cache_t kc = {NULL, NULL};
+    const int64_t kv_rows = B * Hkv * KS;
+    if (kv_rows > 0 && total >= 64 && (double)kv_rows * (double)D * 4.0 <= (double)(1ll << 30)) {
+        kc.kf = (float*)malloc(sizeof(float) * (size_t)(kv_rows * D));
+        kc.vf = (float*)malloc(sizeof(float) * (size_t)(kv_rows * D));
+        if (!kc.kf || !kc.vf) {
+            free(kc.kf);
+            free(kc.vf);
+            kc.kf = kc.vf = NULL;
+        } else {
+#pragma omp parallel for schedule(static)
+            for (int64_t r = 0; r < kv_rows; r++) {
+                const int64_t j = r % KS, bk = r / KS, kvh = bk % Hkv, b = bk / Hkv;
+                const uint16_t* kp = k + b * st.ks_b + kvh * st.ks_h + j * st.ks_s;
+                const uint16_t* vp = v + b * st.vs_b + kvh * st.vs_h + j * st.vs_s;
+                float* kr = kc.kf + r * D;
+                float* vr = kc.vf + r * D;
+                for (int64_t d = 0; d < D; d++) {
+                    kr[d] = h2f(kp[d]);
+                    vr[d] = h2f(vp[d]);
+                }
+                if (has_rope) rope_row(kr, D, rot_cos + j * (D / 2), rot_sin + j * (D / 2), rope_round);
+            }
+        }
+    }
 #pragma omp parallel
     {
         float* qrow = (float*)malloc(sizeof(float) * (size_t)D);
@@ -191,13 +238,15 @@ ORACLE_API int oracle_attention_f16(const uint16_t* q, const uint16_t* k, const 
                 int64_t h = bh % H;
                 int64_t b = bh / H;
                 attend_row_f16(q, k, v, rot_cos, rot_sin, &st, H, Hkv, S, KS, D, scale, causal, has_rope,
-                               window, rope_round, b, h, qi, out + r * D, qrow, krow, pr);
+                               window, rope_round, b, h, qi, out + r * D, qrow, krow, pr, &kc);
             }
         }
         free(qrow);
         free(krow);
         free(pr);
     }
+    free(kc.kf);
+    free(kc.vf);
     return err ? -2 : 0;
 }
 

@@ -1,6 +1,6 @@
 """Builds the reference's own fp64 gate oracles into oracle/_ref/libgate_ref.so.
 
-    python oracle/build_ref.py [REFERENCE_ROOT]
+    python oracle/build_ref.py [REFERENCE_ROOT]   (else $RDNA_REFERENCE_ROOT, else ../reference)
 
 The reference pins its kernels with two CPU oracles written in plain C++ but
 living inside HIP test drivers (tests/hip_forward_gate.hip and
@@ -25,7 +25,21 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 LIB = OUT_DIR / "libgate_ref.so"
-DEFAULT_REF = Path("/root/reference")
+
+
+def reference_root(arg=None):
+    """The reference checkout: an explicit argument, else $RDNA_REFERENCE_ROOT, else a
+    directory named `reference` beside this repository; None when none of them holds
+    the reference's gate drivers."""
+    cands = [arg] if arg else []
+    if os.environ.get("RDNA_REFERENCE_ROOT"):
+        cands.append(os.environ["RDNA_REFERENCE_ROOT"])
+    cands.append(HERE.parent.parent / "reference")
+    for c in cands:
+        root = Path(c)
+        if (root / "tests" / "hip_forward_gate.hip").exists():
+            return root
+    return None
 
 
 def _extract(text: str, start_pattern: str) -> str:
@@ -97,7 +111,11 @@ int8_t gate_int8_quantize(float x, float scale) { return i8gate::quantize(x, sca
 """
 
 
-def build(ref_root: Path = DEFAULT_REF, force: bool = False) -> Path:
+def build(ref_root=None, force: bool = False) -> Path:
+    found = reference_root(ref_root)
+    if found is None:
+        raise FileNotFoundError("reference checkout not found (pass its root or set RDNA_REFERENCE_ROOT)")
+    ref_root = found
     f16_src = ref_root / "tests" / "hip_forward_gate.hip"
     i8_src = ref_root / "tests" / "hip_forward_int8qk_gate.hip"
     if not f16_src.exists() or not i8_src.exists():
@@ -132,5 +150,5 @@ def build(ref_root: Path = DEFAULT_REF, force: bool = False) -> Path:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 and not sys.argv[1].startswith("-") else DEFAULT_REF
+    root = sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("-") else None
     print(build(root, force="--force" in sys.argv))

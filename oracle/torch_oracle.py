@@ -11,7 +11,8 @@ head) ``softmax((q @ k^T) * scale) @ v``) in fp32, extended with:
 * interleaved-pair RoPE of tests/rope.py:29-37 (table row = position);
 * INT8 operands dequantised per tests/hip_forward_int8qk_gate.hip:158-176.
 
-Loops per (batch, kv-head) group and per query-row chunk to bound memory.
+Loops per (batch, kv-head) group and per query-row chunk to bound memory; each
+chunk multiplies only the key columns some of its rows can see.
 """
 import math
 from typing import Optional
@@ -31,13 +32,33 @@ def rope_interleaved(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> t
     return out
 
 
-def _mask(S: int, KS: int, causal: bool, window: int, q0: int, q1: int) -> Optional[torch.Tensor]:
+def _key_span(S: int, KS: int, causal: bool, window: int, q0: int, q1: int):
+    """[lo, hi) of the keys any row in [q0, q1) can see (the whole range without masks)."""
+    if not causal and window <= 0:
+        return 0, KS
+    delta = KS - S
+    hi = KS
+    lo = 0
+    if causal:
+        hi = min(KS, q1 - 1 + delta + 1)
+    if window > 0:
+        if causal:
+            lo = max(0, q0 + delta - window + 1)
+        else:
+            lo = max(0, q0 + delta - window // 2)
+            hi = min(hi, q1 - 1 + delta + window // 2 + 1)
+    return lo, max(lo, hi)
+
+
+def _mask(S: int, KS: int, causal: bool, window: int, q0: int, q1: int, k0: int = 0,
+          k1: Optional[int] = None) -> Optional[torch.Tensor]:
     if not causal and window <= 0:
         return None
+    k1 = KS if k1 is None else k1
     delta = KS - S
     qi = torch.arange(q0, q1).unsqueeze(1)
-    ki = torch.arange(KS).unsqueeze(0)
-    keep = torch.ones(q1 - q0, KS, dtype=torch.bool)
+    ki = torch.arange(k0, k1).unsqueeze(0)
+    keep = torch.ones(q1 - q0, k1 - k0, dtype=torch.bool)
     if causal:
         keep &= ki <= qi + delta
     if window > 0:
@@ -80,8 +101,13 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
                 qq = rope_interleaved(qq, cos, sin)
             for q0 in range(0, S, row_chunk):
                 q1 = min(S, q0 + row_chunk)
-                s = (qq[q0:q1] @ kk.transpose(0, 1)) * scale
-                keep = _mask(S, KS, causal, window, q0, q1)
+                # only the keys some row of the chunk can see (masked scores are -inf,
+                # so dropping whole masked columns changes nothing)
+                k0, k1 = _key_span(S, KS, causal, window, q0, q1)
+                if k1 <= k0:
+                    continue  # no row of the chunk sees a key: output 0
+                s = (qq[q0:q1] @ kk[k0:k1].transpose(0, 1)) * scale
+                keep = _mask(S, KS, causal, window, q0, q1, k0, k1)
                 if keep is not None:
                     s = s.masked_fill(~keep, float("-inf"))
                     empty = ~keep.any(dim=1)
@@ -90,7 +116,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
                     p[empty] = 0.0
                 else:
                     p = torch.softmax(s, dim=-1)
-                out[b, oh, q0:q1] = p @ vv
+                out[b, oh, q0:q1] = p @ vv[k0:k1]
     return out
 
 

@@ -33,8 +33,16 @@ class RDNAttentionError(Exception):
     """Raised for any rdnattention library error."""
 
 
+def _candidate_paths():
+    """Search order of the reference loader (rdnattention/__init__.py:46-67):
+    $RDNATTENTION_LIB, else <source tree>/build/ (a CMake build, which wins in a
+    source checkout), else the package's own lib/ (python -m rdnattention_b200.build)."""
+    name = "librdnattention.so"
+    return [_PKG.parent / "build" / name, _PKG / "lib" / name]
+
+
 def library_path() -> Path:
-    """Where librdnattention.so is loaded from: $RDNATTENTION_LIB, else the in-tree build."""
+    """Where librdnattention.so is loaded from: $RDNATTENTION_LIB, else build/, else lib/."""
     if platform.system() != "Linux":
         raise RDNAttentionError(f"Unsupported platform: {platform.system()} (CUDA build is Linux-only)")
     override = os.environ.get("RDNATTENTION_LIB")
@@ -43,11 +51,12 @@ def library_path() -> Path:
         if not path.exists():
             raise RDNAttentionError(f"RDNATTENTION_LIB points at a missing file: {path}")
         return path
-    path = _PKG / "lib" / "librdnattention.so"
-    if not path.exists():
-        raise RDNAttentionError(
-            f"Could not find librdnattention.so at {path}. Build it first: python -m rdnattention_b200.build")
-    return path
+    for path in _candidate_paths():
+        if path.exists():
+            return path
+    raise RDNAttentionError(
+        "Could not find librdnattention.so in " + ", ".join(str(p.parent) for p in _candidate_paths())
+        + ". Build it first: python -m rdnattention_b200.build (or cmake -B build && cmake --build build)")
 
 
 def _lib_handle():
@@ -79,6 +88,8 @@ def _lib_handle():
         lib.rdna_debug_int8qk_scores.restype = i32
         lib.rdna_debug_read_status.argtypes = [ctypes.POINTER(i32)]
         lib.rdna_debug_read_status.restype = i32
+        lib.rdna_debug_set_wait_test.argtypes = [i32, ctypes.c_uint64]
+        lib.rdna_debug_set_wait_test.restype = i32
         _lib = lib
     return _lib
 
@@ -158,6 +169,15 @@ def _stream_handle(device):
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _on_device(device):
+    """Makes `device` current around a library call: the C side reads the current
+    device for its per-device state (SM count, kernel attributes, the no-alloc
+    workspace address)."""
+    import torch
+
+    return torch.cuda.device(device)
+
+
 def _fp16_forward(query, key, value, is_causal, window_size, rot_cos, rot_sin, out, scale, require_contiguous):
     import torch
 
@@ -178,12 +198,13 @@ def _fp16_forward(query, key, value, is_causal, window_size, rot_cos, rot_sin, o
     ws_bytes = lib.rdna_attention_forward_workspace_size(batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
                                                          has_rope)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=query.device) if ws_bytes else None
-    rc = lib.rdna_attention_forward_ws(
-        query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(), cos_p, sin_p,
-        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
-        batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
-        float(scale), 1 if is_causal else 0, has_rope, int(window_size),
-        ws.data_ptr() if ws is not None else None, ws_bytes, _stream_handle(query.device))
+    with _on_device(query.device):
+        rc = lib.rdna_attention_forward_ws(
+            query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(), cos_p, sin_p,
+            qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
+            batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+            float(scale), 1 if is_causal else 0, has_rope, int(window_size),
+            ws.data_ptr() if ws is not None else None, ws_bytes, _stream_handle(query.device))
     if rc != 0:
         raise RDNAttentionError(f"flash_attn failed: {_last_error()}")
     return out
@@ -248,13 +269,14 @@ def flash_attn_int8qk(query, key, value, q_scale, k_scale, v_scale: float, is_ca
     k_scalar, k_vec = scale_arg(k_scale, "k_scale", (batch, kv_heads, key_seq_len))
     out = torch.empty(query.shape, dtype=torch.float16, device=query.device)
     qs, ks, vs, os_ = query.stride(), key.stride(), value.stride(), out.stride()
-    rc = _lib_handle().rdna_attention_forward_int8qk(
-        query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
-        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
-        batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
-        float(head_dim ** -0.5), q_scalar, k_scalar, float(v_scale),
-        q_vec.data_ptr() if q_vec is not None else None, k_vec.data_ptr() if k_vec is not None else None,
-        1 if is_causal else 0, int(window_size), _stream_handle(query.device))
+    with _on_device(query.device):
+        rc = _lib_handle().rdna_attention_forward_int8qk(
+            query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+            qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
+            batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+            float(head_dim ** -0.5), q_scalar, k_scalar, float(v_scale),
+            q_vec.data_ptr() if q_vec is not None else None, k_vec.data_ptr() if k_vec is not None else None,
+            1 if is_causal else 0, int(window_size), _stream_handle(query.device))
     if rc != 0:
         raise RDNAttentionError(f"flash_attn_int8qk failed: {_last_error()}")
     return out
@@ -288,13 +310,14 @@ def debug_int8qk_scores(query, key, value, q_scale, k_scale, v_scale: float, is_
     out = torch.empty(query.shape, dtype=torch.float16, device=query.device)
     scores = torch.full((batch, heads, seq_len, key_seq_len), -2 ** 31, dtype=torch.int32, device=query.device)
     qs, ks, vs, os_ = query.stride(), key.stride(), value.stride(), out.stride()
-    rc = _lib_handle().rdna_debug_int8qk_scores(
-        query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
-        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
-        batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
-        float(head_dim ** -0.5), q_scalar, k_scalar, float(v_scale),
-        q_vec.data_ptr() if q_vec is not None else None, k_vec.data_ptr() if k_vec is not None else None,
-        1 if is_causal else 0, int(window_size), scores.data_ptr(), _stream_handle(query.device))
+    with _on_device(query.device):
+        rc = _lib_handle().rdna_debug_int8qk_scores(
+            query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+            qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
+            batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+            float(head_dim ** -0.5), q_scalar, k_scalar, float(v_scale),
+            q_vec.data_ptr() if q_vec is not None else None, k_vec.data_ptr() if k_vec is not None else None,
+            1 if is_causal else 0, int(window_size), scores.data_ptr(), _stream_handle(query.device))
     if rc != 0:
         raise RDNAttentionError(f"debug_int8qk_scores failed: {_last_error()}")
     return out, scores
@@ -373,11 +396,12 @@ def quantize_int8_qkv(query, key, value):
     k_scale = torch.empty(batch, kv_heads, key_seq_len, dtype=torch.float32, device=dev)
     v_channel = torch.empty(batch, kv_heads, head_dim, dtype=torch.float32, device=dev)
     qs, ks, vs = query.stride(), key.stride(), value.stride()
-    rc = _lib_handle().rdna_int8_quantize_qkv(
-        query.data_ptr(), key.data_ptr(), value.data_ptr(), qs[0], qs[1], qs[2], ks[0], ks[1], ks[2],
-        vs[0], vs[1], vs[2], batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
-        qi.data_ptr(), ki.data_ptr(), vi.data_ptr(), q_scale.data_ptr(), k_scale.data_ptr(), v_channel.data_ptr(),
-        _stream_handle(dev))
+    with _on_device(dev):
+        rc = _lib_handle().rdna_int8_quantize_qkv(
+            query.data_ptr(), key.data_ptr(), value.data_ptr(), qs[0], qs[1], qs[2], ks[0], ks[1], ks[2],
+            vs[0], vs[1], vs[2], batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+            qi.data_ptr(), ki.data_ptr(), vi.data_ptr(), q_scale.data_ptr(), k_scale.data_ptr(),
+            v_channel.data_ptr(), _stream_handle(dev))
     if rc != 0:
         raise RDNAttentionError(f"quantize_int8_qkv failed: {_last_error()}")
     return qi, ki, vi, q_scale, k_scale, v_channel
@@ -411,12 +435,13 @@ def flash_attn_int8qk_quantized(query, key, value, is_causal: bool = False, wind
     _check_head_dim(head_dim, "flash_attn_int8qk", allowed=SUPPORTED_HEAD_DIMS_INT8)
     out = torch.empty(qi.shape, dtype=torch.float16, device=qi.device)
     qs, ks, vs, os_ = qi.stride(), ki.stride(), vi.stride(), out.stride()
-    rc = _lib_handle().rdna_attention_forward_int8qk_vch(
-        qi.data_ptr(), ki.data_ptr(), vi.data_ptr(), out.data_ptr(),
-        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
-        batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
-        float(head_dim ** -0.5), 1.0, 1.0, float(v_scale), q_scale.data_ptr(), k_scale.data_ptr(),
-        v_channel.data_ptr(), 1 if is_causal else 0, int(window_size), _stream_handle(qi.device))
+    with _on_device(qi.device):
+        rc = _lib_handle().rdna_attention_forward_int8qk_vch(
+            qi.data_ptr(), ki.data_ptr(), vi.data_ptr(), out.data_ptr(),
+            qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
+            batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
+            float(head_dim ** -0.5), 1.0, 1.0, float(v_scale), q_scale.data_ptr(), k_scale.data_ptr(),
+            v_channel.data_ptr(), 1 if is_causal else 0, int(window_size), _stream_handle(qi.device))
     if rc != 0:
         raise RDNAttentionError(f"flash_attn_int8qk failed: {_last_error()}")
     return out

@@ -13,6 +13,7 @@
 
 namespace rdna {
 int debugReadStatus(int32_t* out2, const char** why);
+void debugSetWaitTest(int32_t withhold_block, uint64_t wait_limit_ns);
 }
 
 namespace {
@@ -354,5 +355,10 @@ RDNA_API int32_t rdna_debug_read_status(int32_t* out2) {
         set_error("Debug status failed: %s", why);
         return -3;
     }
+    return 0;
+}
+
+RDNA_API int32_t rdna_debug_set_wait_test(int32_t withhold_block, uint64_t wait_limit_ns) {
+    rdna::debugSetWaitTest(withhold_block, wait_limit_ns);
     return 0;
 }

@@ -77,6 +77,7 @@ struct Params {
     int rope;               // nonzero: rotate Q and K (tables [max(S, KS), D/2] fp32)
     const float* rope_cos;
     const float* rope_sin;
+    int kv_bcast;  // K/V axes broadcast with stride 0 (prefill::KV_BCAST_* bits): coordinate 0
 };
 
 template <int D>
@@ -222,6 +223,8 @@ __global__ void __launch_bounds__(ROPE ? THREADS_ROPE : THREADS, 1) fa_decode_ke
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
+            const int kh = (p.kv_bcast & 2) ? 0 : kvh, kb = (p.kv_bcast & 1) ? 0 : b;  // broadcast axes: coordinate 0
+            const int vh = (p.kv_bcast & 8) ? 0 : kvh, vb = (p.kv_bcast & 4) ? 0 : b;
             int filled[NST] = {0};
             bool ok = true;
             for (int i = 0; i < ntiles; ++i) {
@@ -234,8 +237,8 @@ __global__ void __launch_bounds__(ROPE ? THREADS_ROPE : THREADS, 1) fa_decode_ke
                 const uint32_t dst = smem_u32(ring + s * L::STAGE);
                 const int k0 = (t_begin + i) * KT;
                 for (int bx = 0; bx < L::NBOX; ++bx) {
-                    tma_load_4d(dst + bx * L::BOX_BYTES, &tmK, full_bar(s), bx * L::BOX, k0, kvh, b, pol);
-                    tma_load_4d(dst + L::TILE + bx * L::BOX_BYTES, &tmV, full_bar(s), bx * L::BOX, k0, kvh, b, pol);
+                    tma_load_4d(dst + bx * L::BOX_BYTES, &tmK, full_bar(s), bx * L::BOX, k0, kh, kb, pol);
+                    tma_load_4d(dst + L::TILE + bx * L::BOX_BYTES, &tmV, full_bar(s), bx * L::BOX, k0, vh, vb, pol);
                 }
                 filled[s]++;
             }

@@ -22,10 +22,9 @@
 //   warp 4*NT+3       Q producer (one lane): each item's Q tiles, once the
 //                     previous item's Q K^T MMAs no longer read the buffer.
 //
-// Persistent CTAs (the double-buffered kernels): one CTA per SM loops over
-// work items i, i + gridDim.x, ... (longest first); barrier phases run on
-// across items, so the next item's Q / K / V loads and first Q K^T overlap the
-// current item's last blocks and epilogue.  Other kernels run one item per CTA.
+// One work item per CTA (items longest first for causal masks; the hardware
+// block scheduler balances the tail).  The roles keep phase counters that
+// would run on across items, so a role's loop body is written per item.
 //
 // Two schedules:
 //   * single-buffered S (128-key blocks; INT8, head_dim > 128): per block j
@@ -94,10 +93,20 @@ struct Params {
     // debug (T::DUMP_S kernels): the raw s32 Q K^T of every computed key block,
     // int32 [B, H, S, KS] contiguous
     int32_t* s_dump;
+    // K/V axes broadcast with element stride 0 (KV_BCAST_* bits): their tensor
+    // map has extent 1 there and the load coordinate is 0
+    int kv_bcast;
+    // debug (expired-wait test, off when dbg_withhold < 0): CTA 0 never loads the
+    // K tile of its dbg_withhold-th key block and its waits give up after
+    // dbg_wait_limit_ns, so the wait for that tile expires and the CTA unwinds
+    int dbg_withhold;
+    unsigned long long dbg_wait_limit_ns;
 };
 
+constexpr int KV_BCAST_KB = 1, KV_BCAST_KH = 2, KV_BCAST_VB = 4, KV_BCAST_VH = 8;
+
 template <int D_, int DVMAX_, int BC_, int NT_, int NSK_, int NSV_, bool I8_, bool SDB_ = false,
-          bool DUMP_S_ = false>
+          bool DUMP_S_ = false, bool TWOPASS_ = false>
 struct Traits {
     static constexpr int D = D_;          // QK depth (head_dim)
     static constexpr int DVMAX = DVMAX_;  // output columns per CTA (<= 256)
@@ -108,6 +117,12 @@ struct Traits {
     static constexpr bool I8 = I8_;
     // debug instantiations (INT8): write the raw s32 Q K^T to Params::s_dump
     static constexpr bool DUMP_S = DUMP_S_;
+    // INT8 in two passes over the keys (S double-buffered): pass 1 only finds each
+    // row's max, pass 2 quantises P against that final max, so the s32 P V
+    // accumulator never needs rescaling and no fold into an fp32 O exists (valid
+    // while 127 * 128 * key_seq_len < 2^31; longer sequences take the fold kernel).
+    static constexpr bool TWOPASS = TWOPASS_;
+    static_assert(!TWOPASS || I8_, "two-pass schedule is INT8-only");
     static_assert(!DUMP_S || I8, "score dump is INT8-only");
     // S double-buffered in TMEM: QK(j+2) is issued right after PV(j), while
     // the softmax works on S(j+1) from the other buffer.
@@ -117,20 +132,11 @@ struct Traits {
     // its own issuer (warps WARP_MMA and WARP_MMA + 1), so one tile's barrier
     // waits overlap the other tile's MMA issue.  K/V ring slots are released
     // once every issuer has committed.
-    static constexpr int NI = (SDB && NT == 2) ? 2 : 1;
-    // Persistent CTAs (one per SM, looping over work items) for the
-    // double-buffered kernels: the next item's Q load and first MMAs overlap
-    // the current item's epilogue, and TMEM / barrier setup happens once.
-    // Off by default: with a static item split it measured 2-8 % slower than
-    // one CTA per item, whose order the hardware block scheduler balances.
-#ifndef RDNA_PERSIST
-#define RDNA_PERSIST 0
-#endif
-    static constexpr bool PERSIST = SDB && RDNA_PERSIST;
+    static constexpr int NI = ((SDB || TWOPASS) && NT == 2) ? 2 : 1;
     // Exp-phase token between the two softmax warpgroups, per scheduler: warp
     // w of one tile and warp w of the other (the pair that shares a MUFU) take
     // turns, without waiting for the other schedulers' warps.
-    static constexpr bool TOKEN = NT == 2 && !PERSIST && RDNA_EXP_TOKEN;
+    static constexpr bool TOKEN = NT == 2 && RDNA_EXP_TOKEN;
     // FP16 exponent phase on sm_100's paired fp32 instructions (scale-and-shift
     // FMAs and row sums two at a time: fewer issues on the softmax critical path)
 #ifndef RDNA_F32X2
@@ -144,8 +150,7 @@ struct Traits {
     // Kernels that can rotate Q themselves (one item per CTA: the softmax
     // warps are idle until the first S, so they rotate the Q tile that the
     // first Q K^T waits for); the RoPE pre-pass then only rotates K.
-    static constexpr bool ROPE_Q = SDB && !PERSIST;
-    static_assert(!(SDB && I8), "S double buffering is FP16-only");
+    static constexpr bool ROPE_Q = SDB && !I8;
     static_assert(NSK <= 8 && NSV <= 8 && (!SDB || NSV >= 2), "ring depth");
     static constexpr int ESZ = I8 ? 1 : 2;
     static constexpr int ROW_BYTES = D * ESZ;
@@ -169,21 +174,25 @@ struct Traits {
     // under half the shared memory each), so one CTA's prologue and epilogue
     // overlap the other's main loop.
     static constexpr int MIN_BLOCKS = (NT == 1 && SDB) ? 2 : 1;
-    // Register split: launched at LAUNCH_REGS per thread.
+    // Register split: launched at LAUNCH_REGS per thread (the most __launch_bounds__
+    // allows for THREADS), then moved between warpgroups with setmaxnreg.
     static constexpr bool RESPLIT = NT == 2 || MIN_BLOCKS == 2;
-    static constexpr int LAUNCH_REGS = MIN_BLOCKS == 2 ? 128 : 168;
+    static constexpr int LAUNCH_REGS = MIN_BLOCKS == 2 ? 128 : (65536 / THREADS) / 8 * 8;
     // 128-key blocks hold 128 scores per softmax thread; 64-key blocks (S
     // double-buffered) need far fewer, and the two MMA issuer warps then keep
     // enough registers not to spill.
-    static constexpr int SOFTMAX_REGS = MIN_BLOCKS == 2 ? 184 : SDB ? 176 : 216;
-    static constexpr int CONTROL_REGS = MIN_BLOCKS == 2 ? 72 : SDB ? 152 : 56;
+    // (splits at which ptxas spills nothing, checked by tests/test_resources_cpu.py)
+    static constexpr int SOFTMAX_REGS = MIN_BLOCKS == 2 ? 184 : SDB ? 168 : (I8 && !TWOPASS) ? 208 : 216;
+    static constexpr int CONTROL_REGS = MIN_BLOCKS == 2 ? 72 : SDB ? 168 : (I8 && !TWOPASS) ? 72 : 56;
     static_assert(!RESPLIT || 128 * NT * SOFTMAX_REGS + 128 * CONTROL_REGS <= THREADS * LAUNCH_REGS,
                   "register split exceeds the launch allocation");
 
     // TMEM columns
     static constexpr int S_COL0 = 0;                                 // S(t, b) at (t * NSB + b) * BC
     static constexpr int ACC_COL0 = NT * NSB * BC;                   // INT8 only
-    static constexpr int O_COL0 = I8 ? NT * BC + NT * DVMAX : NT * NSB * BC;
+    // (the two-pass INT8 kernel has no fp32 O in TMEM: its output is ACC / l)
+    static constexpr int O_COL0 = I8 ? NT * NSB * BC + (TWOPASS ? 0 : NT * DVMAX) : NT * NSB * BC;
+    static_assert(!I8 || TWOPASS || !SDB, "the one-pass INT8 kernel keeps S single-buffered");
     static constexpr int TMEM_USED = O_COL0 + NT * DVMAX;
     static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                      : TMEM_USED <= 256 ? 256 : 512;
@@ -191,11 +200,9 @@ struct Traits {
     static_assert(D % BOX == 0 && DVMAX % BOX == 0, "head_dim must tile into boxes");
     static_assert(BC % KSTEP == 0 && BC % 32 == 0, "key block");
 
-    // Output (fp16) staging geometry.  FP16: O uses Q's swizzle and box; it is
-    // staged in Q_t's buffer (one item per CTA) or in its own region
-    // (persistent CTAs, where the next item's Q lands during the epilogue).
-    // INT8: fp16 rows are twice as wide as the int8 Q rows, so O gets its own
-    // 128B-swizzled staging region.
+    // Output (fp16) staging geometry.  FP16: O uses Q's swizzle and box and is
+    // staged in Q_t's buffer.  INT8: fp16 rows are twice as wide as the int8 Q
+    // rows, so O gets its own 128B-swizzled staging region.
     static constexpr int O_SW = I8 ? 128 : SW;
     static constexpr int O_BOX = O_SW / 2;
     static constexpr int O_BOX_BYTES = BM * O_SW;
@@ -204,11 +211,12 @@ struct Traits {
 
     // Shared memory: [misc 1 KB (+ INT8 key scales)][Q tiles][K ring][V ring]
     // (+ INT8 O staging), tiles 1024-aligned.
-    static constexpr int MISC_BYTES = 1024 + (I8 ? NT * 2 * BC * 4 : 0);
+    static constexpr int OFF_KSCALE = 1024;  // INT8: [NT][2][BC] fp32 per-key scales
+    static constexpr int MISC_BYTES = I8 ? OFF_KSCALE + NT * 2 * BC * 4 : 1024;
     static constexpr int OFF_Q = ((MISC_BYTES + 1023) / 1024) * 1024;
     static constexpr int OFF_K = OFF_Q + NT * Q_TILE;
     static constexpr int OFF_V = OFF_K + NSK * K_TILE;
-    static constexpr bool OWN_STAGE = I8 || PERSIST;
+    static constexpr bool OWN_STAGE = I8;
     static constexpr int OFF_O = OWN_STAGE ? OFF_V + NSV * V_TILE : OFF_Q;
     static constexpr int O_STRIDE = OWN_STAGE ? O_TILE : Q_TILE;  // staging bytes between tiles
     static constexpr int SMEM_BYTES = OFF_V + NSV * V_TILE + (OWN_STAGE ? NT * O_TILE : 0) + 1024;  // + align slack
@@ -365,14 +373,10 @@ __device__ __forceinline__ void tile_blocks(const Params& p, int row0, bool vali
     e = hi / T::BC + 1;
 }
 
-// The r-th work item of this CTA, or -1 past the end.  Items are numbered
-// longest first; rounds alternate direction (CTA c takes item c in even
-// rounds and gridDim.x-1-c in odd ones), so a static split of causal work
-// stays balanced.  With one CTA per item (gridDim.x == n_items) round 0 is
-// the CTA's own item.
+// The work item of this CTA (one item per CTA, items numbered longest first),
+// or -1 past the end.  r counts the CTA's items (always 0 here).
 __device__ __forceinline__ int item_at(const Params& p, int r) {
-    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
-    const int64_t item = static_cast<int64_t>(r) * G + ((r & 1) ? G - 1 - c : c);
+    const int64_t item = static_cast<int64_t>(r) * gridDim.x + blockIdx.x;
     return item < p.n_items ? static_cast<int>(item) : -1;
 }
 
@@ -430,7 +434,15 @@ __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
 template <class T>
 __device__ __forceinline__ void load_s_row(uint32_t taddr, uint32_t* r) {
     if constexpr (T::BC == 128) {
-        tmem_ld_x128(taddr, r);
+        if constexpr (T::LAUNCH_REGS <= 128) {
+            // two 64-column loads, one wait: a 128-register destination does not fit
+            // a kernel launched at 128 registers per thread
+            tmem_ld_x64_nowait(taddr, r);
+            tmem_ld_x64_nowait(taddr + 64, r + 64);
+            tmem_wait_ld();
+        } else {
+            tmem_ld_x128(taddr, r);
+        }
     } else if constexpr (T::BC == 64) {
         tmem_ld_x64(taddr, r);
     } else {
@@ -538,8 +550,8 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
     int n_o = 0;   // earlier items in which tile t accumulated O (O_FULL / O_EMPTY phases)
     int n_st = 0;  // earlier O stores of tile t (EPI / STG_FREE phases)
 
-    // non-persistent kernels: exactly one item (a trip count the compiler can see)
-    for (int n_it = 0; T::PERSIST || n_it < 1; ++n_it) {
+    // exactly one item per CTA (a trip count the compiler can see)
+    for (int n_it = 0; n_it < 1; ++n_it) {
     const int item = item_at(p, n_it);
     if (item < 0) break;
     const Item I = make_item<T>(p, item);
@@ -569,8 +581,8 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
 
     // INT8 state
     float rowscale = 1.f;
-    bool oflushed = false;
-    float pq_acc = 0.f;  // bound on sum(Pq) held in ACC since the last fold
+    bool oflushed = false;  // O holds folded blocks
+    float pq_acc = 0.f;     // bound on sum(Pq) held in ACC since the last fold
     float* ksbuf = nullptr;
     const bool kvec = T::I8 && p.k_vec != nullptr;
     if constexpr (T::I8) {
@@ -578,7 +590,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         if (p.q_vec != nullptr && q < p.S) qs = p.q_vec[(static_cast<int64_t>(w.b) * p.H + w.head[t]) * p.S + q];
         rowscale = qs * sl2;
         if (!kvec) rowscale *= p.k_scale;
-        ksbuf = reinterpret_cast<float*>(smem + 1024) + t * 2 * T::BC;
+        ksbuf = reinterpret_cast<float*>(smem + T::OFF_KSCALE) + t * 2 * T::BC;
     }
 
     // per-key K scales of the next block are fetched one block ahead, so the
@@ -612,16 +624,19 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         if (aborted) continue;
         tc_fence_after();
 
-        uint32_t raw[T::BC];
-        load_s_row<T>(tS, raw);
         if constexpr (T::DUMP_S) {
-            if (q < p.S) {
-                int32_t* dst = p.s_dump + ((static_cast<int64_t>(w.b) * p.H + w.head[t]) * p.S + q) * p.KS;
+            // debug: the raw s32 scores, re-read 16 columns at a time (warp-wide loads)
+            int32_t* dst = p.s_dump + ((static_cast<int64_t>(w.b) * p.H + w.head[t]) * p.S + q) * p.KS;
+            for (int c0 = 0; c0 < T::BC; c0 += 16) {
+                uint32_t d16[16];
+                tmem_ld_x16(tS + c0, d16);
 #pragma unroll
-                for (int c = 0; c < T::BC; ++c)
-                    if (j * T::BC + c < p.KS) dst[j * T::BC + c] = static_cast<int32_t>(raw[c]);
+                for (int c = 0; c < 16; ++c)
+                    if (q < p.S && j * T::BC + c0 + c < p.KS) dst[j * T::BC + c0 + c] = static_cast<int32_t>(d16[c]);
             }
         }
+        uint32_t raw[T::BC];
+        load_s_row<T>(tS, raw);
         float* x = reinterpret_cast<float*>(raw);
         const bool full = block_full<T>(p, row0, j);
         const int lo = klo - j * T::BC, hi = khi - j * T::BC;
@@ -721,48 +736,8 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
                 tmem_wait_st();
             }
         } else {
-            // INT8: the s32 accumulator holds sum(Pq * V) quantised against the running
-            // max.  A warp folds it into the fp32 O when any of its rows' max moves, and
-            // before a row's |ACC| can reach 2^22 (the limit of the conversion below):
-            // after this block's PV, ACC holds at most pq_acc + 128 * BC + BC/2 < 2^15
-            // times max|V| <= 128.  Every lane folds (factor 1 where its max did not
-            // move), so the fold has no per-element selects.
-            const bool flush = rescale || (it > 0 && pq_acc >= T::PQ_FOLD);
-            if (__any_sync(0xffffffffu, flush)) {
-                const float c = rescale ? corr : 1.f;
-                const float psc = p.pv_scale * c;
-                const uint64_t psc2 = f2(psc, psc), c2 = f2(c, c), mb2 = f2(-12582912.0f, -12582912.0f);
-                for (int c0 = 0; c0 < dv; c0 += 32) {
-                    uint32_t acc[32], o[32];
-                    tmem_ld_x32(tACC + c0, acc);
-                    if (oflushed) {
-                        tmem_ld_x32(tO + c0, o);
-#pragma unroll
-                        for (int i = 0; i < 32; i += 2) {
-                            const uint64_t af = fadd2(f2(i2f_biased(acc[i]), i2f_biased(acc[i + 1])), mb2);
-                            const uint64_t oc = fmul2(f2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), c2);
-                            float a0, a1;
-                            f2_split(ffma2(af, psc2, oc), a0, a1);
-                            o[i] = __float_as_uint(a0);
-                            o[i + 1] = __float_as_uint(a1);
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 2) {
-                            const uint64_t af = fadd2(f2(i2f_biased(acc[i]), i2f_biased(acc[i + 1])), mb2);
-                            float a0, a1;
-                            f2_split(fmul2(af, psc2), a0, a1);
-                            o[i] = __float_as_uint(a0);
-                            o[i + 1] = __float_as_uint(a1);
-                        }
-                    }
-                    tmem_st_x32(tO + c0, o);
-                    tmem_zero_x32(tACC + c0);
-                }
-                tmem_wait_st();
-                oflushed = true;
-                pq_acc = 0.f;
-            }
+            // INT8: the accumulator fold runs after the exponent phase (below), when the
+            // block's scores no longer hold registers; P V(j) waits for both anyway
         }
 
         // P = exp2(s*scale*log2e - m); the row sum uses the unrounded values
@@ -860,7 +835,52 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         lsum = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         l += lsum;
         // sum(Pq) <= 127 * sum(p) + BC/2; the factor 128 covers the f16 partial sums' rounding
-        if constexpr (T::I8) pq_acc += fmaf(lsum, 128.f, 0.5f * T::BC);
+        if constexpr (T::I8) {
+            // INT8: the s32 accumulator holds sum(Pq * V) quantised against the running
+            // max.  A warp folds it into the fp32 O when any of its rows' max moves, and
+            // before a row's |ACC| can reach 2^22 (the limit of the conversion below):
+            // after this block's PV, ACC holds at most pq_acc + 128 * BC + BC/2 < 2^15
+            // times max|V| <= 128.  Every lane folds (factor 1 where its max did not
+            // move), so the fold has no per-element selects; 16 columns at a time keep
+            // the fold's registers beside the block's scores.
+            const bool flush = rescale || (it > 0 && pq_acc >= T::PQ_FOLD);
+            if (__any_sync(0xffffffffu, flush)) {
+                const float c = rescale ? corr : 1.f;
+                const float psc = p.pv_scale * c;
+                const uint64_t psc2 = f2(psc, psc), c2 = f2(c, c), mb2 = f2(-12582912.0f, -12582912.0f);
+                for (int c0 = 0; c0 < dv; c0 += 16) {
+                    uint32_t acc[16], o[16];
+                    tmem_ld_x16(tACC + c0, acc);
+                    if (oflushed) {
+                        tmem_ld_x16(tO + c0, o);
+#pragma unroll
+                        for (int i = 0; i < 16; i += 2) {
+                            const uint64_t af = fadd2(f2(i2f_biased(acc[i]), i2f_biased(acc[i + 1])), mb2);
+                            const uint64_t oc = fmul2(f2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), c2);
+                            float a0, a1;
+                            f2_split(ffma2(af, psc2, oc), a0, a1);
+                            o[i] = __float_as_uint(a0);
+                            o[i + 1] = __float_as_uint(a1);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 2) {
+                            const uint64_t af = fadd2(f2(i2f_biased(acc[i]), i2f_biased(acc[i + 1])), mb2);
+                            float a0, a1;
+                            f2_split(fmul2(af, psc2), a0, a1);
+                            o[i] = __float_as_uint(a0);
+                            o[i + 1] = __float_as_uint(a1);
+                        }
+                    }
+                    tmem_st_x16(tO + c0, o);
+                }
+                for (int c0 = 0; c0 < dv; c0 += 32) tmem_zero_x32(tACC + c0);
+                tmem_wait_st();
+                oflushed = true;
+                pq_acc = 0.f;
+            }
+            pq_acc += fmaf(lsum, 128.f, 0.5f * T::BC);
+        }
         if constexpr (T::TOKEN) {
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(Bars::EXPD + t * 4 + wq));
@@ -897,6 +917,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
                 uint32_t ov[32];
                 tmem_ld_x32(tO + c0, ov);
                 if constexpr (T::I8) {
+                    // O (the folded blocks, if any) plus the blocks in ACC since the last fold
                     uint32_t acc[32];
                     tmem_ld_x32(tACC + c0, acc);
 #pragma unroll
@@ -947,8 +968,7 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
             for (int bx = 0; bx < nbox; ++bx)
                 tma_store_4d(tmO, smem_u32(stage + bx * T::O_BOX_BYTES), dv0 + bx * T::O_BOX, row0, w.head[t], w.b);
             bulk_commit();
-            // one item per CTA: staging in Q's buffer, wait here; persistent:
-            // the next epilogue (or the exit below) waits
+            // FP16 stages O in Q's buffer: wait here; INT8 waits before the exit
             if constexpr (!T::OWN_STAGE) bulk_wait_read_all();
         }
     }
@@ -974,7 +994,7 @@ __device__ void producer_q_role(const Params& p, const CUtensorMap* tmQ, uint8_t
     prefetch_tmap(tmQ);
     const uint64_t pol_q = policy_evict_first();
     int qfill = 0;
-    for (int r = 0; T::PERSIST || r < 1; ++r) {
+    for (int r = 0; r < 1; ++r) {
         const int item = item_at(p, r);
         if (item < 0) break;
         const Work w = decode_work<T>(p, item);
@@ -1004,26 +1024,37 @@ __device__ void producer_kv_role(const Params& p, const CUtensorMap* tmK, const 
     int kfill[T::NSK] = {0};
     int vfill[T::NSV] = {0};
     bool ok = true;
-    int i = 0;  // K/V blocks loaded so far
-    for (int n = 0; ok && (T::PERSIST || n < 1); ++n) {
+    int i = 0;   // K blocks loaded so far
+    int iv = 0;  // V blocks loaded so far
+    for (int n = 0; ok && n < 1; ++n) {
         const int item = item_at(p, n);
         if (item < 0) break;
         const Item I = make_item<T>(p, item);
         const Work& w = I.w;
         const int nbox_v = I.dv / T::BOX;
-        for (int j = I.jlo; j < I.jhi; ++j, ++i) {
+        const int kh = (p.kv_bcast & KV_BCAST_KH) ? 0 : w.kvh, kb = (p.kv_bcast & KV_BCAST_KB) ? 0 : w.b;
+        const int vh = (p.kv_bcast & KV_BCAST_VH) ? 0 : w.kvh, vb = (p.kv_bcast & KV_BCAST_VB) ? 0 : w.b;
+        // two-pass INT8: every K block twice (pass 1 finds the row maxima), V in pass 2 only
+        const int N = I.jhi - I.jlo;
+        for (int u = 0; u < (T::TWOPASS ? 2 * N : N); ++u, ++i) {
+            const int j = I.jlo + (u < N ? u : u - N);
             const int ks = i % T::NSK, kn = i / T::NSK;
             if (!mbar_wait(bar(Bars::K_EMPTY + ks), (kn & 1) ^ 1, ab, SITE_PROD_KEMPTY)) {
                 ok = false;
                 break;
             }
-            mbar_arrive_expect_tx(bar(Bars::K_FULL + ks), T::K_TILE);
-            const uint32_t kdst = smem_u32(smem + T::OFF_K + ks * T::K_TILE);
-            for (int bx = 0; bx < T::NBOX; ++bx)
-                tma_load_4d(kdst + bx * T::K_BOX_BYTES, tmK, bar(Bars::K_FULL + ks), bx * T::BOX, j * T::BC, w.kvh,
-                            w.b, pol_kv);
-            kfill[ks]++;
-            const int vs = i % T::NSV, vn = i / T::NSV;
+            if (p.dbg_withhold == i && blockIdx.x == 0) {
+                // debug launch: this tile never arrives (its consumer's wait expires)
+            } else {
+                mbar_arrive_expect_tx(bar(Bars::K_FULL + ks), T::K_TILE);
+                const uint32_t kdst = smem_u32(smem + T::OFF_K + ks * T::K_TILE);
+                for (int bx = 0; bx < T::NBOX; ++bx)
+                    tma_load_4d(kdst + bx * T::K_BOX_BYTES, tmK, bar(Bars::K_FULL + ks), bx * T::BOX, j * T::BC, kh,
+                                kb, pol_kv);
+                kfill[ks]++;
+            }
+            if (T::TWOPASS && u < N) continue;
+            const int vs = iv % T::NSV, vn = iv / T::NSV;
             if (!mbar_wait(bar(Bars::V_EMPTY + vs), (vn & 1) ^ 1, ab, SITE_PROD_VEMPTY)) {
                 ok = false;
                 break;
@@ -1032,8 +1063,9 @@ __device__ void producer_kv_role(const Params& p, const CUtensorMap* tmK, const 
             const uint32_t vdst = smem_u32(smem + T::OFF_V + vs * T::V_TILE);
             for (int bx = 0; bx < nbox_v; ++bx)
                 tma_load_4d(vdst + bx * T::K_BOX_BYTES, tmV, bar(Bars::V_FULL + vs), I.dv0 + bx * T::BOX,
-                            j * T::BC, w.kvh, w.b, pol_kv);
+                            j * T::BC, vh, vb, pol_kv);
             vfill[vs]++;
+            ++iv;
         }
     }
     if (!ok) {
@@ -1116,14 +1148,15 @@ __device__ void mma_role_sdb(const Params& p, uint8_t* smem, uint32_t tmem, cons
     int kc = 0, vc = 0, n = 0;
     int g[2] = {0, 0}, n_o[2] = {0, 0};
     bool ok = true;
-    for (; ok && (T::PERSIST || n < 1); ++n) {
+    for (; ok && n < 1; ++n) {
         const int item = item_at(p, n);
         if (item < 0) break;
         const Item I = make_item<T>(p, item);
         const int* ta = I.ta;
         const int* te = I.te;
         const int jlo = I.jlo, jhi = I.jhi;
-        const uint32_t idesc_pv = instr_desc(1u, 0u, 1u, BM, static_cast<uint32_t>(I.dv));
+        const uint32_t idesc_pv =
+            instr_desc(T::I8 ? 2u : 1u, T::I8 ? 1u : 0u, 1u, BM, static_cast<uint32_t>(I.dv));
         if (!mbar_wait(bar(Bars::Q_FULL), n & 1, ab, SITE_MMA_Q)) {
             ok = false;
             break;
@@ -1179,6 +1212,7 @@ __device__ void mma_role_sdb(const Params& p, uint8_t* smem, uint32_t tmem, cons
                         ok = false;
                         break;
                     }
+
                     if (it == 0 && n_o[t] > 0 &&
                         !mbar_wait(bar(Bars::O_EMPTY + t), (n_o[t] - 1) & 1, ab, SITE_MMA_OEMPTY)) {
                         ok = false;
@@ -1222,7 +1256,7 @@ __device__ void mma_role(const Params& p, uint8_t* smem, uint32_t tmem, const Ab
     int kc = 0, vc = 0, n = 0;
     int pc[2] = {0, 0}, n_o[2] = {0, 0};
     bool ok = true;
-    for (; ok && (T::PERSIST || n < 1); ++n) {
+    for (; ok && n < 1; ++n) {
         const int item = item_at(p, n);
         if (item < 0) break;
         const Item I = make_item<T>(p, item);
@@ -1306,6 +1340,310 @@ __device__ void mma_role(const Params& p, uint8_t* smem, uint32_t tmem, const Ab
     mbar_wait_drain(bar(Bars::DRAIN), 0);
 }
 
+// ------------------------------------------------- INT8, two passes over K
+// Softmax warpgroup of tile t for T::TWOPASS.  Key blocks are visited twice in
+// one sequence of S buffers (virtual block v = pass * n + it, S in buffer v & 1):
+//   pass 1: S -> the row's exact max over every visible key (no exponentials);
+//           the arrival on P_FULL only hands the S buffer back to the MMA issuer;
+//   pass 2: S -> p = exp2(s * scale * log2(e) - max) <= 1, Pq = round(127 p)
+//           written over S for the int8 P V MMA, row sum of the unrounded p.
+// Pq is quantised against the row's global max (the reference gate's own
+// semantics, tests/hip_forward_int8qk_gate.hip:69-120), so the s32 accumulator
+// is never rescaled and O = ACC * v_scale / 127 / l at the end.
+template <class T>
+__device__ void softmax_role_i8x2(const Params& p, const CUtensorMap* tmO, int t, uint8_t* smem, uint32_t tmem,
+                                  const Abort& ab) {
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int wq = warp % 4;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS0 = tmem + lane_base + T::S_COL0 + t * T::NSB * T::BC;
+    const uint32_t tACC = tmem + lane_base + T::ACC_COL0 + t * T::DVMAX;
+    const uint32_t bars = smem_u32(smem);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+    bool aborted = false;
+
+    const int item = item_at(p, 0);
+    if (item < 0) return;
+    const Item I = make_item<T>(p, item);
+    const Work& w = I.w;
+    if (!w.valid[t]) return;  // uniform for the warpgroup
+    const int dv = I.dv, dv0 = I.dv0;
+    const int row0 = w.row0[t];
+    const int q = row0 + r;
+    const int a = I.ta[t], e = I.te[t];
+    const int n = e - a;
+    int klo, khi;
+    row_keys(p, q, klo, khi);
+    const int other_iters = T::TOKEN ? I.te[1 - t] - I.ta[1 - t] : 0;
+
+    const bool kvec = p.k_vec != nullptr;
+    float qs = p.q_scale;
+    if (p.q_vec != nullptr && q < p.S) qs = p.q_vec[(static_cast<int64_t>(w.b) * p.H + w.head[t]) * p.S + q];
+    float rowscale = qs * p.scale_log2;
+    if (!kvec) rowscale *= p.k_scale;
+    const bool neg = rowscale < 0.f;  // then x is negated so that max(x) * |rowscale| is the max
+    const float ars = fabsf(rowscale);
+    float* ksbuf = reinterpret_cast<float*>(smem + T::OFF_KSCALE) + t * 2 * T::BC;
+    const float* kvec_row = kvec ? p.k_vec + (static_cast<int64_t>(w.b) * p.Hkv + w.kvh) * p.KS : nullptr;
+    auto load_ks = [&](int jb) {
+        const int key = jb * T::BC + r;
+        return (kvec && r < T::BC && jb < e && key < p.KS) ? __ldg(kvec_row + key) : 0.f;
+    };
+    float ks_next = load_ks(a);
+
+    float m = -INFINITY;  // the row's max of s * rowscale (log2 domain), complete after pass 1
+    float l = 0.f;
+    for (int v = 0; v < 2 * n; ++v) {
+        const bool second = v >= n;
+        const int it = second ? v - n : v;
+        const int j = a + it;
+        if (kvec) {
+            // stage this block's per-key scales; buffer (v & 1) is reused every second block
+            const int buf = v & 1;
+            if (r < T::BC) ksbuf[buf * T::BC + r] = ks_next;
+            mbar_arrive(bar(Bars::KS_FULL + 2 * t + buf));
+            ks_next = load_ks(it + 1 < n ? j + 1 : a);
+            if (!aborted && !warp_wait(bar(Bars::KS_FULL + 2 * t + buf), (v >> 1) & 1, ab, SITE_SM_KS))
+                aborted = true;
+        }
+        const int sb = v % T::NSB;
+        const uint32_t tS = tS0 + sb * T::BC;
+        if (!aborted && !warp_wait(bar(Bars::S_FULL + t * T::NSB + sb), (v / T::NSB) & 1, ab, SITE_SM_S))
+            aborted = true;
+        if (aborted) continue;
+        tc_fence_after();
+
+        if constexpr (T::DUMP_S) {
+            if (second) {
+                // debug: the raw s32 scores, read 16 columns at a time (warp-wide loads)
+                int32_t* dst = p.s_dump + ((static_cast<int64_t>(w.b) * p.H + w.head[t]) * p.S + q) * p.KS;
+                for (int c0 = 0; c0 < T::BC; c0 += 16) {
+                    uint32_t d16[16];
+                    tmem_ld_x16(tS + c0, d16);
+#pragma unroll
+                    for (int c = 0; c < 16; ++c)
+                        if (q < p.S && j * T::BC + c0 + c < p.KS)
+                            dst[j * T::BC + c0 + c] = static_cast<int32_t>(d16[c]);
+                }
+            }
+        }
+        uint32_t raw[T::BC];
+        load_s_row<T>(tS, raw);
+        // s32 -> float on the ALU (exact: |q.k| <= 127*127*D < 2^22), times the key
+        // scale, negated for a negative row scale, masked outside the row's keys
+        float* x = reinterpret_cast<float*>(raw);
+        const uint64_t mb2 = f2(-12582912.0f, -12582912.0f);
+        const float* ksb = ksbuf + (v & 1) * T::BC;
+        if (kvec) {
+#pragma unroll
+            for (int c = 0; c < T::BC; c += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(ksb + c);
+                const uint64_t u0 = fadd2(f2(i2f_biased(raw[c]), i2f_biased(raw[c + 1])), mb2);
+                const uint64_t u1 = fadd2(f2(i2f_biased(raw[c + 2]), i2f_biased(raw[c + 3])), mb2);
+                f2_split(fmul2(u0, f2(k4.x, k4.y)), x[c], x[c + 1]);
+                f2_split(fmul2(u1, f2(k4.z, k4.w)), x[c + 2], x[c + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < T::BC; c += 2)
+                f2_split(fadd2(f2(i2f_biased(raw[c]), i2f_biased(raw[c + 1])), mb2), x[c], x[c + 1]);
+        }
+        if (neg) {
+#pragma unroll
+            for (int c = 0; c < T::BC; ++c) x[c] = -x[c];
+        }
+        if (!block_full<T>(p, row0, j)) {
+            const int lo = klo - j * T::BC, hi = khi - j * T::BC;
+#pragma unroll
+            for (int c = 0; c < T::BC; ++c)
+                if (c < lo || c > hi) x[c] = -INFINITY;
+        }
+
+        if (!second) {
+            float mx = row_max<T::BC>(x) * ars;
+            if (mx != mx) mx = -INFINITY;  // fully masked with a zero row scale
+            m = fmaxf(m, mx);
+        } else {
+            // exponent phases of the two tiles alternate on each scheduler's MUFU
+            if constexpr (T::TOKEN) {
+                const int need = it - 1 + t;
+                if (need >= 0 && need < other_iters &&
+                    !warp_wait(bar(Bars::EXPD + (1 - t) * 4 + wq), need & 1, ab, SITE_SM_TOKEN)) {
+                    aborted = true;
+                    continue;
+                }
+            }
+            // p two at a time in half precision (P keeps 7 bits): fma(p, 127, 1024) in
+            // fp16 has unit spacing, so its low byte is round(p * 127) (to nearest even; the
+            // reference's lround differs only at exact .5 ties).  Row sums accumulate in 8
+            // f16x2 partials (<= BC / 8 values each) and finish in fp32.
+            const float neg_m = (m == -INFINITY) ? 0.f : -m;
+            const uint64_t ars2 = f2(ars, ars), nm2 = f2(neg_m, neg_m);
+            constexpr uint32_t k127 = 0x57F057F0u;   // (127, 127) in f16x2
+            constexpr uint32_t k1024 = 0x64006400u;  // (1024, 1024)
+            uint32_t hs[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+            for (int c0 = 0; c0 < T::BC; c0 += 32) {
+                uint32_t pk[8];
+#pragma unroll
+                for (int c = 0; c < 32; c += 4) {
+                    float a0, a1, a2, a3;
+                    f2_split(ffma2(f2(x[c0 + c], x[c0 + c + 1]), ars2, nm2), a0, a1);
+                    f2_split(ffma2(f2(x[c0 + c + 2], x[c0 + c + 3]), ars2, nm2), a2, a3);
+                    const uint32_t e0 = ex2_h2(pack_half2(a0, a1));
+                    const uint32_t e1 = ex2_h2(pack_half2(a2, a3));
+                    hs[(c >> 2) & 7] = hadd2(hs[(c >> 2) & 7], hadd2(e0, e1));
+                    pk[c / 4] = pack_half_low_bytes(hfma2(e0, k127, k1024), hfma2(e1, k127, k1024));
+                }
+                tmem_st_x8(tS + c0 / 4, pk);
+            }
+            float ls[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const __half2 h = *reinterpret_cast<const __half2*>(&hs[i]);
+                ls[i] = __low2float(h) + __high2float(h);
+            }
+            l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+            if constexpr (T::TOKEN) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(Bars::EXPD + t * 4 + wq));
+            }
+            tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(Bars::P_FULL + t * T::NSB + sb));
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    const bool has_blocks = n > 0;
+    if (!aborted && has_blocks && !warp_wait(bar(Bars::O_FULL + t), 0, ab, SITE_SM_O)) aborted = true;
+    if (!aborted) tc_fence_after();
+    uint8_t* stage = smem + T::OFF_O + t * T::O_STRIDE;
+    if (!aborted) {
+        // O = ACC * (v_scale / 127) / l (times the per-channel V scale when given)
+        const float f = (l > 0.f) ? p.pv_scale / l : 0.f;
+        for (int c0 = 0; c0 < dv; c0 += 32) {
+            float o[32];
+            if (has_blocks) {
+                uint32_t acc[32];
+                tmem_ld_x32(tACC + c0, acc);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[i] = static_cast<float>(static_cast<int>(acc[i])) * f;
+                if (p.v_chan != nullptr) {
+                    // per-channel V dequantisation, folded in before the one fp16 rounding
+                    const float* vc = p.v_chan + (static_cast<int64_t>(w.b) * p.Hkv + w.kvh) * T::D + dv0 + c0;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= __ldg(vc + i);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[i] = 0.f;
+            }
+#pragma unroll
+            for (int g4 = 0; g4 < 4; ++g4) {
+                uint4 u;
+                u.x = pack_half2(o[8 * g4 + 0], o[8 * g4 + 1]);
+                u.y = pack_half2(o[8 * g4 + 2], o[8 * g4 + 3]);
+                u.z = pack_half2(o[8 * g4 + 4], o[8 * g4 + 5]);
+                u.w = pack_half2(o[8 * g4 + 6], o[8 * g4 + 7]);
+                const int col = c0 + 8 * g4;
+                const int box = col / T::O_BOX;
+                const int chunk = (col % T::O_BOX) / 8;
+                *reinterpret_cast<uint4*>(stage + box * T::O_BOX_BYTES + swz_off<T::O_SW>(r, chunk)) = u;
+            }
+        }
+        fence_proxy_async_smem();
+    }
+    mbar_arrive(bar(Bars::EPI + t));
+    if (r == 0) {
+        if (!aborted && mbar_wait(bar(Bars::EPI + t), 0, ab, SITE_SM_EPI) && !*ab.flag) {
+            const int nbox = dv / T::O_BOX;
+            for (int bx = 0; bx < nbox; ++bx)
+                tma_store_4d(tmO, smem_u32(stage + bx * T::O_BOX_BYTES), dv0 + bx * T::O_BOX, row0, w.head[t], w.b);
+            bulk_commit();
+        }
+        bulk_wait_all();  // the store has landed before the CTA exits
+    }
+}
+
+// MMA issuer of the two-pass INT8 kernel (one per tile): Q K^T over the tile's
+// key blocks twice, in the virtual-block order of softmax_role_i8x2, with S
+// double-buffered; S(v + 2) is issued once the softmax has handed S(v) back
+// (pass 1) or once P V(v) has been issued after it (pass 2: tcgen05 MMAs of
+// one thread run in order, so P V(v) reads P before Q K^T(v + 2) overwrites).
+// K ring slots are shared by both issuers and freed after both commit.
+template <class T>
+__device__ void mma_role_i8x2(const Params& p, uint8_t* smem, uint32_t tmem, const Abort& ab, int issuer) {
+    const int t = T::NI == 1 ? 0 : issuer;  // tile of this issuer (NT == 1: issuer 0 only)
+    const uint32_t bars = smem_u32(smem);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+    const Descs<T> dz(smem);
+    bool ok = true;
+    const int item = item_at(p, 0);
+    if (item >= 0) {
+        const Item I = make_item<T>(p, item);
+        const int jlo = I.jlo, N = I.jhi - I.jlo;
+        const int ta = I.ta[t], te = I.te[t];
+        const uint32_t idesc_pv = instr_desc(2u, 1u, 1u, BM, static_cast<uint32_t>(I.dv));
+        // virtual block u over the union of the tiles' ranges, twice; this tile's own
+        // virtual block index (its S buffer sequence) is vt(u)
+        auto active = [&](int u) { const int j = jlo + (u % N); return ta <= j && j < te; };
+        auto vt = [&](int u) { const int j = jlo + (u % N); return (u >= N ? te - ta : 0) + (j - ta); };
+        ok = mbar_wait(bar(Bars::Q_FULL), 0, ab, SITE_MMA_Q);
+        if (ok) tc_fence_after();
+        int kc = 0, vc = 0;
+        auto issue_k = [&](int u) -> bool {  // Q K^T of virtual block u (K slot kc), if this tile has it
+            const int ks = kc % T::NSK;
+            if (!mbar_wait(bar(Bars::K_FULL + ks), (kc / T::NSK) & 1, ab, SITE_MMA_K)) return false;
+            tc_fence_after();
+            if (active(u)) {
+                const int sb = vt(u) % T::NSB;
+                issue_qk<T>(dz, tmem, t, ks, sb);
+                tc_commit(bar(Bars::S_FULL + t * T::NSB + sb));
+            }
+            tc_commit(bar(Bars::K_EMPTY + ks));
+            kc++;
+            return true;
+        };
+        for (int u = 0; ok && u < T::NSB && u < 2 * N; ++u) ok = issue_k(u);
+        for (int u = 0; ok && u < 2 * N; ++u) {
+            const bool second = u >= N;
+            int vs = 0;
+            if (second) {
+                vs = vc % T::NSV;
+                if (!mbar_wait(bar(Bars::V_FULL + vs), (vc / T::NSV) & 1, ab, SITE_MMA_V)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (active(u)) {
+                const int v = vt(u), sb = v % T::NSB;
+                if (!mbar_wait(bar(Bars::P_FULL + t * T::NSB + sb), (v / T::NSB) & 1, ab, SITE_MMA_P)) {
+                    ok = false;
+                    break;
+                }
+                if (second) {
+                    tc_fence_after();
+                    const int j = jlo + (u - N);
+                    issue_pv<T>(dz, tmem, t, vs, j > ta, idesc_pv, sb);
+                    if (j == te - 1) tc_commit(bar(Bars::O_FULL + t));
+                }
+            }
+            if (second) {
+                tc_commit(bar(Bars::V_EMPTY + vs));
+                vc++;
+            }
+            if (u + T::NSB < 2 * N) ok = issue_k(u + T::NSB);
+        }
+        if (ok) tc_commit(bar(Bars::Q_EMPTY));
+    }
+    tc_commit(bar(Bars::DRAIN + issuer));
+    mbar_wait_drain(bar(Bars::DRAIN + issuer), 0);
+}
+
 // ---------------------------------------------------------------- kernel
 template <class T>
 __global__ void __launch_bounds__(T::THREADS, T::MIN_BLOCKS)
@@ -1361,7 +1699,7 @@ __global__ void __launch_bounds__(T::THREADS, T::MIN_BLOCKS)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const Abort ab{abort_flag};
+    const Abort ab{abort_flag, (p.dbg_withhold >= 0 && blockIdx.x == 0) ? p.dbg_wait_limit_ns : kWaitLimitNs};
 
     if constexpr (T::RESPLIT) {
         if (warp < 4 * T::NT)
@@ -1370,7 +1708,10 @@ __global__ void __launch_bounds__(T::THREADS, T::MIN_BLOCKS)
             regs_decrease<T::CONTROL_REGS>();
     }
     if (warp < 4 * T::NT) {
-        softmax_role<T>(p, &tmO, warp / 4, smem, tmem, ab);
+        if constexpr (T::TWOPASS)
+            softmax_role_i8x2<T>(p, &tmO, warp / 4, smem, tmem, ab);
+        else
+            softmax_role<T>(p, &tmO, warp / 4, smem, tmem, ab);
         tc_fence_before();
     } else if (warp == T::WARP_PROD) {
         if (sm100::lane_id() == 0) producer_kv_role<T>(p, &tmK, &tmV, smem, ab);
@@ -1380,14 +1721,18 @@ __global__ void __launch_bounds__(T::THREADS, T::MIN_BLOCKS)
         __syncwarp();
     } else if (warp == T::WARP_MMA) {
         if (sm100::lane_id() == 0) {
-            if constexpr (T::SDB)
+            if constexpr (T::TWOPASS)
+                mma_role_i8x2<T>(p, smem, tmem, ab, 0);
+            else if constexpr (T::SDB)
                 mma_role_sdb<T>(p, smem, tmem, ab, 0);
             else
                 mma_role<T>(p, smem, tmem, ab);
         }
         __syncwarp();
     } else if (T::NI == 2 && warp == T::WARP_MMA + 1) {
-        if constexpr (T::SDB) {
+        if constexpr (T::TWOPASS) {
+            if (sm100::lane_id() == 0) mma_role_i8x2<T>(p, smem, tmem, ab, 1);
+        } else if constexpr (T::SDB) {
             if (sm100::lane_id() == 0) mma_role_sdb<T>(p, smem, tmem, ab, 1);
         }
         __syncwarp();

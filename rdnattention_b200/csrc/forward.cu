@@ -90,6 +90,26 @@ struct Common {
 
 bool fits_i32(int64_t s) { return s >= INT32_MIN && s <= INT32_MAX; }
 
+// K/V axes broadcast with element stride 0 (prefill::KV_BCAST_* bits).  Their
+// tensor maps get extent 1 on that axis and the kernels load coordinate 0.
+int kv_bcast_bits(const Common& c) {
+    int m = 0;
+    if (c.KS == 0) return 0;
+    if (c.B > 1 && c.ks[0] == 0) m |= prefill::KV_BCAST_KB;
+    if (c.Hkv > 1 && c.ks[1] == 0) m |= prefill::KV_BCAST_KH;
+    if (c.B > 1 && c.vs[0] == 0) m |= prefill::KV_BCAST_VB;
+    if (c.Hkv > 1 && c.vs[1] == 0) m |= prefill::KV_BCAST_VH;
+    return m;
+}
+
+// A [batch, heads, seq, head_dim] K or V view for a tensor map: broadcast axes shrink to extent 1.
+uint64_t bc_extent(uint64_t n, bool bcast) { return bcast ? 1u : n; }
+
+// Debug settings of the calling thread for the expired-wait test
+// (rdna_debug_set_wait_test): withheld K tile and shortened wait limit.
+thread_local int g_dbg_withhold = -1;
+thread_local unsigned long long g_dbg_wait_limit_ns = 0;
+
 const char* check_common(const Common& c) {
     // with key_seq_len == 0 K and V are never read (an empty tensor may have a null pointer)
     if (c.q == nullptr || c.o == nullptr || (c.KS > 0 && (c.k == nullptr || c.v == nullptr)))
@@ -110,13 +130,18 @@ const char* check_common(const Common& c) {
         const uint64_t* ext = t == 0 ? ext_q : ext_kv;
         for (int a = 0; a < 3; ++a) {
             if (ext[a] <= 1) continue;
-            if (in[t][a] <= 0) return "strides must be positive (broadcast or reversed axes are not supported)";
+            // K/V may broadcast one tensor over the batch or head axis (stride 0, e.g. one
+            // KV head shared by every query head); everything else needs positive strides
+            if (in[t][a] == 0 && t > 0 && a < 2) continue;
+            if (in[t][a] <= 0)
+                return "strides must be positive (stride 0 only on the K/V batch and head axes; reversed axes are "
+                       "not supported)";
             if (in[t][a] % align_in != 0) return "batch/head/seq strides must be multiples of 16 bytes";
         }
     }
     for (int a = 0; a < 3; ++a) {
         if (ext_q[a] <= 1) continue;
-        if (c.os[a] <= 0) return "strides must be positive (broadcast or reversed axes are not supported)";
+        if (c.os[a] <= 0) return "output strides must be positive";
         if (c.os[a] % 8 != 0) return "output batch/head/seq strides must be multiples of 16 bytes";
     }
     return nullptr;
@@ -133,10 +158,18 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
     const View4 vq{c.q, {c.D, c.S, c.H, c.B}, {c.qs[2], c.qs[1], c.qs[0]}};
     // key_seq_len == 0: K/V are never read; give them a valid 1-row map
     const bool nokv = c.KS == 0;
-    const View4 vk{nokv ? c.q : c.k, {c.D, nokv ? 1u : c.KS, nokv ? 1u : c.Hkv, nokv ? 1u : c.B},
+    p.kv_bcast = kv_bcast_bits(c);
+    const int bc = p.kv_bcast;
+    const View4 vk{nokv ? c.q : c.k,
+                   {c.D, nokv ? 1u : c.KS, nokv ? 1u : bc_extent(c.Hkv, bc & KV_BCAST_KH),
+                    nokv ? 1u : bc_extent(c.B, bc & KV_BCAST_KB)},
                    {c.ks[2], c.ks[1], c.ks[0]}};
-    const View4 vv{nokv ? c.q : c.v, {c.D, nokv ? 1u : c.KS, nokv ? 1u : c.Hkv, nokv ? 1u : c.B},
+    const View4 vv{nokv ? c.q : c.v,
+                   {c.D, nokv ? 1u : c.KS, nokv ? 1u : bc_extent(c.Hkv, bc & KV_BCAST_VH),
+                    nokv ? 1u : bc_extent(c.B, bc & KV_BCAST_VB)},
                    {c.vs[2], c.vs[1], c.vs[0]}};
+    p.dbg_withhold = g_dbg_withhold;
+    p.dbg_wait_limit_ns = g_dbg_wait_limit_ns;
     const View4 vo{c.o, {c.D, c.S, c.H, c.B}, {c.os[2], c.os[1], c.os[0]}};
     const char* e = nullptr;
     if ((e = make_map(&tmQ, vq, dt, T::ESZ, T::BOX, BM, sw)) ||
@@ -174,20 +207,9 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
     if (items > INT32_MAX) return fail(err, "problem too large for one launch");
     p.n_items = static_cast<int>(items);
 
-    // Persistent kernels: one CTA per SM, each looping over items i, i + grid, ...
-    // (the item order is longest-first, so the strided split stays balanced).
-    // Their shared-memory request is at least half the SM's, so two CTAs never
-    // share an SM (and its 512 TMEM columns).
-    int64_t grid = items;
-    int smem_bytes = T::SMEM_BYTES;
-    if constexpr (T::PERSIST) {
-        int dev = 0, sms = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (grid > sms) grid = sms;
-        constexpr int kHalfSm = 116 * 1024;
-        if (smem_bytes < kHalfSm) smem_bytes = kHalfSm;
-    }
+    // one CTA per work item
+    const int64_t grid = items;
+    const int smem_bytes = T::SMEM_BYTES;
 
     auto kern = fa_prefill_kernel<T>;
     cudaError_t ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
@@ -231,8 +253,7 @@ int dispatch_f16_dim(char* err, const Common& c, const prefill::Params& p, cudaS
     } else if constexpr (D <= 128) {
         // two 128-row tiles per CTA, 64-key blocks, S double-buffered in TMEM
         // (2 tiles x 2 buffers x 64 columns + 2 x D columns of O <= 512)
-        // persistent kernels give shared memory to a separate O staging buffer
-        constexpr int stages = D <= 64 ? 6 : D <= 96 ? 5 : (RDNA_PERSIST ? 3 : 4);
+        constexpr int stages = D <= 64 ? 6 : D <= 96 ? 5 : 4;
         return launch_prefill<Traits<D, D, 64, 2, stages, stages, false, true>>(err, c, p, st, dt);
     } else if constexpr (D <= 256) {
         // one tile per CTA (TMEM holds one O of up to 256 columns), 64-key blocks
@@ -391,9 +412,15 @@ int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
 
     CUtensorMap tmK, tmV;
     const bool nokv = a.keySeqLen == 0;
+    p.kv_bcast = kv_bcast_bits(f16_common(a));
+    const int bc = p.kv_bcast;
     const uint64_t e1 = nokv ? 1 : a.keySeqLen, e2 = nokv ? 1 : a.numKvHeads, e3 = nokv ? 1 : a.batchSize;
-    const View4 vk{nokv ? a.q : a.k, {a.headDim, e1, e2, e3}, {a.kStrideS, a.kStrideH, a.kStrideB}};
-    const View4 vv{nokv ? a.q : a.v, {a.headDim, e1, e2, e3}, {a.vStrideS, a.vStrideH, a.vStrideB}};
+    const View4 vk{nokv ? a.q : a.k,
+                   {a.headDim, e1, bc_extent(e2, bc & prefill::KV_BCAST_KH), bc_extent(e3, bc & prefill::KV_BCAST_KB)},
+                   {a.kStrideS, a.kStrideH, a.kStrideB}};
+    const View4 vv{nokv ? a.q : a.v,
+                   {a.headDim, e1, bc_extent(e2, bc & prefill::KV_BCAST_VH), bc_extent(e3, bc & prefill::KV_BCAST_VB)},
+                   {a.vStrideS, a.vStrideH, a.vStrideB}};
     const char* e = nullptr;
     if ((e = make_map(&tmK, vk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 64, KT, CU_TENSOR_MAP_SWIZZLE_128B)) ||
         (e = make_map(&tmV, vv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 64, KT, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -503,7 +530,9 @@ int forwardF16(const ForwardParams& a, void* stream) {
 // file-scope array, reserved on every device that loads the library's module
 // until the process exits.  In host code the name below is only a host-side
 // stand-in; its device address comes from cudaGetSymbolAddress, taken once
-// per device with that device current, on the first call there.  Every call
+// per device with that device current, on the first call there (so calls
+// after cudaDeviceReset on that device, which reloads the module, are not
+// supported: the cached address may no longer be the array's).  Every call
 // shares the array: the RoPE pre-pass overwrites every byte the attention
 // kernel reads before it is read, so nothing needs clearing, but calls that
 // overlap on the GPU (other streams, other threads) race on it.
@@ -519,6 +548,11 @@ void* g_noalloc_ptr[kMaxDevices] = {};
 size_t noAllocWorkspaceLimit() { return kNoAllocWorkspaceBytes; }
 
 int forwardF16NoAlloc(const ForwardParams& a, void* stream) {
+    {
+        // argument errors first, so a malformed call gets its own message
+        Common c = f16_common(a);
+        if (int rc = f16_validate(c, a)) return rc;
+    }
     const size_t need = f16_workspace_bytes(a);
     if (need > kNoAllocWorkspaceBytes) {
         char msg[160];
@@ -571,15 +605,25 @@ int int8_forward(const ForwardParamsInt8QK& a, int32_t* s_dump, void* stream) {
     p.s_dump = s_dump;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     constexpr CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    // head_dim 64: one pass over 128-key blocks, two query tiles per CTA (S 2 x 128 + ACC
+    // 2 x 64 + O 2 x 64 = 512 TMEM columns), the s32 accumulator folded into the fp32 O
+    // when a row max moves.  head_dim 128, up to kTwoPassMaxKeys keys: two passes (row
+    // maxima, then P against the final max), so the accumulator is never rescaled and
+    // needs no O in TMEM, which leaves room for two tiles (S 2 x 128 + ACC 2 x 128); longer
+    // key ranges take the one-pass kernel with one tile (S + ACC + O = 384 columns).
+    constexpr uint32_t kTwoPassMaxKeys = 131072;  // 127 * 128 * keys < 2^31: no s32 overflow
+    const bool two = a.keySeqLen <= kTwoPassMaxKeys;
+    using namespace prefill;
     if (s_dump != nullptr) {
         // debug instantiations: the same kernels plus the score dump
         if (a.headDim == 64)
-            return launch_prefill<prefill::Traits<64, 64, 128, 2, 4, 4, true, false, true>>(g_err_i8, c, p, st, dt);
-        return launch_prefill<prefill::Traits<128, 128, 128, 1, 3, 3, true, false, true>>(g_err_i8, c, p, st, dt);
+            return launch_prefill<Traits<64, 64, 128, 2, 4, 4, true, false, true>>(g_err_i8, c, p, st, dt);
+        return two ? launch_prefill<Traits<128, 128, 128, 2, 3, 3, true, false, true, true>>(g_err_i8, c, p, st, dt)
+                   : launch_prefill<Traits<128, 128, 128, 1, 3, 3, true, false, true>>(g_err_i8, c, p, st, dt);
     }
-    if (a.headDim == 64)
-        return launch_prefill<prefill::Traits<64, 64, 128, 2, 4, 4, true>>(g_err_i8, c, p, st, dt);
-    return launch_prefill<prefill::Traits<128, 128, 128, 1, 3, 3, true>>(g_err_i8, c, p, st, dt);
+    if (a.headDim == 64) return launch_prefill<Traits<64, 64, 128, 2, 4, 4, true>>(g_err_i8, c, p, st, dt);
+    return two ? launch_prefill<Traits<128, 128, 128, 2, 3, 3, true, false, false, true>>(g_err_i8, c, p, st, dt)
+               : launch_prefill<Traits<128, 128, 128, 1, 3, 3, true>>(g_err_i8, c, p, st, dt);
 }
 }  // namespace
 
@@ -642,6 +686,11 @@ int quantizeInt8QKV(const QuantizeInt8Params& a, void* stream) {
     const cudaError_t ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(g_err_i8, "%s", cudaGetErrorString(ce));
     return 0;
+}
+
+void debugSetWaitTest(int32_t withhold_block, uint64_t wait_limit_ns) {
+    g_dbg_withhold = withhold_block;
+    g_dbg_wait_limit_ns = withhold_block >= 0 ? wait_limit_ns : 0;
 }
 
 const char* lastError() { return g_err_f16[0] ? g_err_f16 : nullptr; }

@@ -72,7 +72,8 @@ RDNA_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 struct Abort {
-    volatile int* flag;  // shared, CTA-wide
+    volatile int* flag;                 // shared, CTA-wide
+    uint64_t limit_ns = kWaitLimitNs;   // per-wait limit (a debug launch may shorten it)
 };
 
 }  // namespace sm100
@@ -117,7 +118,7 @@ RDNA_DEV bool mbar_wait(uint32_t bar, uint32_t parity, const Abort& ab, int site
     while (true) {
         if (mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) return true;
         if (*ab.flag) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > ab.limit_ns) {
             record_error(ab, site);
             return false;
         }

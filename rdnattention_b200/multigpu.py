@@ -34,16 +34,34 @@ def _split(n: int, world: int, rank: int):
 
 
 def plan(batch: int, kv_heads: int, world: int, rank: int) -> Shard:
-    """Batch-major when every rank gets whole batch elements (batch >= world), else
-    split the KV-head groups (batch < world).  Uneven counts give the first ranks
-    one more unit; a rank may own nothing when units < world."""
+    """The rank's rectangle of (batch, KV-head) units.  Batch-major when every rank gets
+    whole batch elements (batch >= world), else KV-head groups when they cover the ranks
+    (kv_heads >= world); otherwise a grid of wb x wg ranks splits both axes, chosen to
+    keep the most ranks busy and then to balance the units per rank (B=2, Hkv=3 on 4
+    ranks: 2 x 2).  Uneven counts give the first ranks one more unit; ranks outside the
+    grid (fewer units than ranks) own nothing."""
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world of {world}")
-    if batch >= world or kv_heads < world:
+    if batch >= world:
         b0, b1 = _split(batch, world, rank)
         return Shard("batch", b0, b1, 0, kv_heads)
-    g0, g1 = _split(kv_heads, world, rank)
-    return Shard("kv_head", 0, batch, g0, g1)
+    if kv_heads >= world:
+        g0, g1 = _split(kv_heads, world, rank)
+        return Shard("kv_head", 0, batch, g0, g1)
+    best = None
+    for wb in range(1, min(batch, world) + 1):
+        wg = min(kv_heads, world // wb)
+        busy = wb * wg
+        cost = -(-batch // wb) * -(-kv_heads // wg)
+        key = (-busy, cost, -wb)
+        if best is None or key < best[0]:
+            best = (key, wb, wg)
+    _, wb, wg = best
+    if rank >= wb * wg:
+        return Shard("batch", 0, 0, 0, 0)
+    b0, b1 = _split(batch, wb, rank // wg)
+    g0, g1 = _split(kv_heads, wg, rank % wg)
+    return Shard("batch" if b1 - b0 > 1 else "kv_head", b0, b1, g0, g1)
 
 
 def local_views(q, k, v, shard: Shard):

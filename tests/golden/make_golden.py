@@ -1,7 +1,7 @@
 """Generates the golden fixtures in tests/golden/*.npz from the REFERENCE's own
 oracle code.  Run in a container where the reference checkout is present:
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]   (default /root/reference)
+    python tests/golden/make_golden.py [REFERENCE_ROOT]   (else $RDNA_REFERENCE_ROOT, else ../reference)
 
 Sources of truth, all executed unmodified from the reference checkout:
 
@@ -278,7 +278,11 @@ def make_quant(ref_root):
 
 
 def main():
-    ref_root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    from oracle.build_ref import reference_root
+
+    ref_root = reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
+    if ref_root is None:
+        raise SystemExit("reference checkout not found (pass its root or set RDNA_REFERENCE_ROOT)")
     make_dense_fp32(ref_root)
     make_head_dim(ref_root)
     make_rope(ref_root)

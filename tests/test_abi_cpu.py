@@ -66,7 +66,9 @@ def _fwd(**kw):
     (dict(qs=(64 * 8 * 64, 8 * 64, 2 ** 33)), "exceeds int32 range"),
     (dict(q=18), "16-byte aligned"),
     (dict(ks=(64 * 8 * 64, 8 * 64, 68)), "multiples of 16 bytes"),
-    (dict(vs=(64 * 8 * 64, 0, 64)), "strides must be positive"),
+    (dict(vs=(64 * 8 * 64, -64 * 64, 64)), "strides must be positive"),
+    (dict(qs=(64 * 8 * 64, 0, 64)), "strides must be positive"),
+    (dict(os=(64 * 8 * 64, 0, 64)), "output strides must be positive"),
     (dict(rope=1), "rot_cos/rot_sin is null"),
     (dict(rope=1, cos=20, sin=32), "16-byte aligned"),
 ])

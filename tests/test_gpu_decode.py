@@ -24,7 +24,7 @@ def _device():
 
 
 def _cache(B, Hkv, KS, D, g):
-    """KV cache stored [B, KS, Hkv, D] (BASELINE config 5 layout), viewed [B, Hkv, KS, D]."""
+    """KV cache stored [B, KS, Hkv, D], viewed [B, Hkv, KS, D] through strides."""
     kb = torch.randn(B, KS, Hkv, D, generator=g).half()
     vb = torch.randn(B, KS, Hkv, D, generator=g).half()
     return kb, vb
@@ -38,7 +38,7 @@ def _check(got, ref):
 
 
 @pytest.mark.parametrize("B,H,Hkv,S,KS,D,causal,window", [
-    (4, 64, 8, 1, 32768, 128, False, -1),   # config 5 shape at B=4
+    (4, 64, 8, 1, 32768, 128, False, -1),   # decode B64 Hq64 Hkv8 KS32768 shape at B=4
     (2, 8, 2, 1, 300, 64, False, -1),        # key tail, D=64
     (3, 16, 4, 4, 1000, 128, True, -1),      # few-token decode, causal
     (2, 8, 8, 1, 777, 128, False, -1),       # MHA decode
@@ -71,7 +71,7 @@ def test_decode_contiguous_cache_matches_strided():
 
 
 def test_decode_full_config5_sampled():
-    """BASELINE config 5 at full size (8.6 GB cache), sampled query heads vs the oracle."""
+    """Decode at B=64, Hq=64, Hkv=8, KS=32768, D=128 (8.6 GB cache), sampled query heads vs the oracle."""
     B, H, Hkv, KS, D = 64, 64, 8, 32768, 128
     g = torch.Generator(device="cuda").manual_seed(5)
     q = torch.randn(B, H, 1, D, generator=g, device="cuda", dtype=torch.float16)
@@ -91,7 +91,7 @@ def test_decode_full_config5_sampled():
 
 
 @pytest.mark.parametrize("B,H,Hkv,S,KS,D,causal,window,theta", [
-    (2, 32, 8, 1, 4096, 128, False, -1, 500000.0),  # GQA decode step, BASELINE config 2 theta
+    (2, 32, 8, 1, 4096, 128, False, -1, 500000.0),  # GQA decode step, theta 5e5
     (2, 8, 2, 4, 1000, 64, True, -1, 10000.0),      # few tokens, causal, D=64
     (1, 16, 1, 1, 3000, 128, False, 512, 1e6),      # MQA, two-sided window
     (1, 4, 4, 1, 33, 128, False, -1, 10000.0),      # key tail (zero-filled rows past KS)

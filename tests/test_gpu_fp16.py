@@ -126,7 +126,7 @@ def test_golden_fixtures(family):
 
 
 def test_baseline_config1_tolerance_gate():
-    """B=1,H=8,S=512,D=64, N(0,1) fp16, vs the fp32 oracle:
+    """MHA B=1,H=8,S=512,D=64 non-causal, N(0,1) fp16, vs the fp32 oracle:
     max-abs <= 2e-3 and mean-abs <= 2e-4."""
     g = torch.Generator().manual_seed(0)
     q = torch.randn(1, 8, 512, 64, generator=g).half()
@@ -148,23 +148,39 @@ def _sampled_rows(B, H, S, n, seed):
     return np.array(sorted(rows), dtype=np.int64)
 
 
-@pytest.mark.parametrize("cfg", ["cfg2", "cfg4a", "cfg4b"])
-def test_full_size_configs_sampled_rows(cfg):
-    """BASELINE configs 2 / 4a / 4b at full size; a row sample is checked against the
-    fp64 oracle (rotate-half RoPE via channel permutation, see _rotate_half_inputs)."""
-    if cfg == "cfg2":
-        B, H, Hkv, S, D, causal, window, theta = 4, 32, 8, 4096, 128, True, -1, 500000.0
-    elif cfg == "cfg4a":
-        B, H, Hkv, S, D, causal, window, theta = 1, 32, 8, 16384, 128, True, 4096, 1e6
-    else:
-        B, H, Hkv, S, D, causal, window, theta = 1, 32, 8, 8192, 128, False, 2048, 1e6
+def _unit_rows(H, Hkv, S, b, kvh):
+    """Flat row indices ((b * H + h) * S + q) of every row of one (batch, KV-head) unit:
+    the G query heads of KV head kvh, all S rows."""
+    G = H // Hkv
+    heads = np.arange(kvh * G, (kvh + 1) * G, dtype=np.int64)
+    return ((b * H + heads)[:, None] * S + np.arange(S, dtype=np.int64)[None, :]).reshape(-1)
+
+
+# Llama-3-8B-shaped prefill workloads at full size: causal GQA S=4096 (RoPE 5e5),
+# causal window 4096 at S=16384 and two-sided +-1024 at S=8192 (RoPE 1e6).
+FULL_SIZE = {
+    "gqa_causal_b4_s4096": (4, 32, 8, 4096, 128, True, -1, 500000.0),
+    "window4096_causal_s16384": (1, 32, 8, 16384, 128, True, 4096, 1e6),
+    "window_pm1024_s8192": (1, 32, 8, 8192, 128, False, 2048, 1e6),
+}
+
+
+@pytest.mark.parametrize("cfg", sorted(FULL_SIZE))
+def test_full_size_configs_whole_unit_and_sampled_rows(cfg):
+    """The benchmarked prefill shapes at full size, against the fp64 oracle with
+    max-abs <= 2e-3 and mean-abs <= 2e-4: every row of one whole (batch, KV-head) unit
+    (the last batch element's last KV head for the causal GQA shape, whose causal
+    diagonal tiles run last; KV head 0 of the window shapes, every row of which
+    crosses a window edge) plus a random row sample over all units."""
+    B, H, Hkv, S, D, causal, window, theta = FULL_SIZE[cfg]
     g = torch.Generator().manual_seed(0)
     q = torch.randn(B, H, S, D, generator=g).half()
     k = torch.randn(B, Hkv, S, D, generator=g).half()
     v = torch.randn(B, Hkv, S, D, generator=g).half()
     cos, sin = rope_tables(S, D, theta)
     got = _run(q, k, v, causal, window, cos, sin)
-    rows = _sampled_rows(B, H, S, 96, seed=1)
+    unit = _unit_rows(H, Hkv, S, B - 1, Hkv - 1) if causal and window <= 0 else _unit_rows(H, Hkv, S, 0, 0)
+    rows = np.union1d(unit, _sampled_rows(B, H, S, 96, seed=1))
     ref = c_oracle.attention_f16(q, k, v, causal=causal, window=window, rot_cos=cos, rot_sin=sin, rows=rows)
     err = (got.reshape(-1, D)[torch.from_numpy(rows)].double() - ref).abs()
     assert err.max().item() <= 2e-3, err.max().item()
@@ -172,7 +188,7 @@ def test_full_size_configs_sampled_rows(cfg):
 
 
 def test_rotate_half_equivalence():
-    """BASELINE configs 2/4 name rotate-half RoPE; the ABI is interleaved pairs
+    """The Llama-shaped prefill workloads name rotate-half RoPE; the ABI is interleaved pairs
     (docs/api.md:92-93).  Permuting Q and K channels (2i <- i, 2i+1 <- i+D/2)
     turns one into the other and leaves Q K^T unchanged."""
     B, H, Hkv, S, D = 1, 4, 2, 200, 128
@@ -203,7 +219,7 @@ def test_rotate_half_equivalence():
 
 
 def test_strided_kv_decode_layout():
-    """K/V stored [B, KS, Hkv, D] (BASELINE config 5 layout) passed with strides."""
+    """K/V stored [B, KS, Hkv, D] (a KV-cache layout) passed with strides."""
     B, H, Hkv, S, KS, D = 2, 16, 4, 3, 700, 128
     g = torch.Generator().manual_seed(9)
     q = torch.randn(B, H, S, D, generator=g).half()
@@ -264,3 +280,33 @@ def test_runs_on_non_default_stream():
     s.synchronize()
     ref = c_oracle.attention_f16(q.cpu(), q.cpu(), q.cpu())
     assert rel_rms(out.cpu(), ref) < 3e-3
+
+
+@pytest.mark.parametrize("S,KS,causal,rope,axis", [
+    (300, 300, True, True, "head"),     # prefill, RoPE pre-pass reading the broadcast K
+    (257, 700, False, False, "head"),   # prefill, cross-attention
+    (1, 1000, False, False, "head"),    # decode kernel
+    (200, 200, True, False, "batch"),   # one K/V shared by every batch element
+])
+def test_kv_stride_zero_broadcast(S, KS, causal, rope, axis):
+    """K/V broadcast with element stride 0 on the head (MQA through a GQA-shaped call) or
+    batch axis, as the reference's int64 strides allow (src/rdna/fa2_forward_f16.hip:885-894):
+    the same result as the call on the materialised tensors."""
+    B, H, Hkv, D = 2, 8, 4, 128
+    g = torch.Generator().manual_seed(S + KS)
+    q = torch.randn(B, H, S, D, generator=g).half()
+    if axis == "head":
+        k1 = torch.randn(B, 1, KS, D, generator=g).half()
+        v1 = torch.randn(B, 1, KS, D, generator=g).half()
+    else:
+        k1 = torch.randn(1, Hkv, KS, D, generator=g).half()
+        v1 = torch.randn(1, Hkv, KS, D, generator=g).half()
+    k, v = k1.expand(B, Hkv, KS, D), v1.expand(B, Hkv, KS, D)
+    cos, sin = rope_tables(max(S, KS), D) if rope else (None, None)
+    kd, vd = k1.cuda().expand(B, Hkv, KS, D), v1.cuda().expand(B, Hkv, KS, D)
+    assert 0 in kd.stride()[:2] and 0 in vd.stride()[:2]
+    got = R.flash_attn_strided(q.cuda(), kd, vd, is_causal=causal, rot_cos=None if cos is None else cos.cuda(),
+                               rot_sin=None if sin is None else sin.cuda()).cpu()
+    ref = c_oracle.attention_f16(q, k.contiguous(), v.contiguous(), causal=causal, rot_cos=cos, rot_sin=sin)
+    err = (got.double() - ref).abs()
+    assert err.max().item() <= 2e-3 and err.mean().item() <= 2e-4

@@ -13,13 +13,22 @@ import torch.multiprocessing as mp
 from rdnattention_b200.multigpu import flash_attn_sharded, local_views, pieces, plan
 
 
-@pytest.mark.parametrize("B,Hkv,world", [(4, 8, 2), (1, 8, 2), (3, 2, 2), (1, 1, 2), (8, 8, 8), (2, 3, 4), (5, 8, 8)])
+@pytest.mark.parametrize("B,Hkv,world", [(4, 8, 2), (1, 8, 2), (3, 2, 2), (1, 1, 2), (8, 8, 8), (2, 3, 4), (5, 8, 8),
+                                         (3, 3, 8), (2, 2, 8), (4, 8, 8)])
 def test_plan_covers_every_unit_once(B, Hkv, world):
     seen = torch.zeros(B, Hkv, dtype=torch.int32)
     for r in range(world):
         s = plan(B, Hkv, world, r)
         seen[s.b0:s.b1, s.g0:s.g1] += 1
     assert torch.equal(seen, torch.ones_like(seen))
+
+
+@pytest.mark.parametrize("B,Hkv,world,busy", [(2, 3, 4, 4), (4, 8, 8, 8), (1, 8, 8, 8), (3, 2, 4, 4), (2, 2, 8, 4),
+                                           (1, 1, 2, 1), (3, 3, 8, 6)])
+def test_plan_keeps_ranks_busy(B, Hkv, world, busy):
+    """Neither axis alone covering the ranks no longer idles them: both axes are split."""
+    owned = [plan(B, Hkv, world, r) for r in range(world)]
+    assert sum((s.b1 - s.b0) * (s.g1 - s.g0) > 0 for s in owned) == busy
 
 
 def test_local_views_are_strided_views():

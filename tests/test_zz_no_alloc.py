@@ -60,8 +60,21 @@ def lib():
     return _lib()
 
 
+def _pool_bytes():
+    """(used, reserved) bytes of the current device's default stream-ordered memory pool,
+    through the CUDA runtime (cudaMemPoolAttrUsedMemCurrent / ReservedMemCurrent)."""
+    rt = ctypes.CDLL("libcudart.so.12")
+    pool = ctypes.c_void_p()
+    assert rt.cudaDeviceGetDefaultMemPool(ctypes.byref(pool), torch.cuda.current_device()) == 0
+    used, reserved = ctypes.c_uint64(), ctypes.c_uint64()
+    assert rt.cudaMemPoolGetAttribute(pool, 7, ctypes.byref(used)) == 0
+    assert rt.cudaMemPoolGetAttribute(pool, 5, ctypes.byref(reserved)) == 0
+    return used.value, reserved.value
+
+
 def test_noalloc_matches_allocating_entry_point_twice(lib):
-    shapes = [(1, 8, 2, 512, 512, 128, True, 500000.0), (2, 4, 4, 300, 700, 64, False, 10000.0)]
+    shapes = [(1, 8, 2, 512, 512, 128, True, 500000.0), (2, 4, 4, 300, 700, 64, False, 10000.0),
+              (1, 4, 2, 200, 300, 256, True, 10000.0)]  # head_dim 256: rotated Q in the array too
     for seed, (B, H, Hkv, S, KS, D, causal, theta) in enumerate(shapes):
         g = torch.Generator(device="cuda").manual_seed(100 + seed)
         q = torch.randn(B, H, S, D, generator=g, device="cuda", dtype=torch.float16)
@@ -72,10 +85,38 @@ def test_noalloc_matches_allocating_entry_point_twice(lib):
         out = torch.full_like(q, float("nan"))
         scale = D ** -0.5
         assert _call(lib.rdna_attention_forward, q, k, v, ref, cos, sin, causal, scale) == 0, lib.rdna_get_error()
+        torch.cuda.synchronize()
+        pool_before, torch_before = _pool_bytes(), torch.cuda.memory_allocated()
         assert _call(lib.rdna_attention_forward_noalloc, q, k, v, out, cos, sin, causal, scale) == 0, \
             lib.rdna_get_error()
         torch.cuda.synchronize()
+        # nothing was taken from the stream-ordered pool or from torch's allocator
+        assert _pool_bytes() == pool_before
+        assert torch.cuda.memory_allocated() == torch_before
         assert torch.isfinite(out).all()
+        assert (out.double() - ref.double()).abs().max().item() <= 2e-3
+
+
+def test_noalloc_workspace_limit_is_exact(lib):
+    """8 KV heads, head_dim 128, 16384 keys: exactly the 32 MiB of rotated K the array
+    holds (head_dim <= 128 rotates Q inside the kernel) -- accepted and correct; one key
+    more is rejected with -3."""
+    B, H, Hkv, S, D = 1, 8, 8, 128, 128
+    for KS, ok in ((16384, True), (16385, False)):
+        g = torch.Generator(device="cuda").manual_seed(KS)
+        q = torch.randn(B, H, S, D, generator=g, device="cuda", dtype=torch.float16)
+        k = torch.randn(B, Hkv, KS, D, generator=g, device="cuda", dtype=torch.float16)
+        v = torch.randn(B, Hkv, KS, D, generator=g, device="cuda", dtype=torch.float16)
+        cos, sin = _tables(KS, D, 500000.0)
+        out = torch.empty_like(q)
+        rc = _call(lib.rdna_attention_forward_noalloc, q, k, v, out, cos, sin, False, D ** -0.5)
+        if not ok:
+            assert rc == -3 and "exceeds the fixed" in lib.rdna_get_error().decode()
+            continue
+        assert rc == 0, lib.rdna_get_error()
+        ref = torch.empty_like(q)
+        assert _call(lib.rdna_attention_forward, q, k, v, ref, cos, sin, False, D ** -0.5) == 0
+        torch.cuda.synchronize()
         assert (out.double() - ref.double()).abs().max().item() <= 2e-3
 
 
