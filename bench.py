@@ -49,6 +49,9 @@ CONFIGS = {
               causal=True, window=-1, theta=500000.0, kind="fp16"),
     "3": dict(workload="cfg3_int8_b8_h16_s2048_d64_pertoken_qk_perchannel_v", B=8, H=16, Hkv=16, S=2048, KS=2048,
               D=64, causal=False, window=-1, theta=None, kind="int8"),
+    # INT8 at head_dim 128 (same scheme as config 3): the two-pass kernel
+    "3h128": dict(workload="int8_b4_h16_s2048_d128_pertoken_qk_perchannel_v", B=4, H=16, Hkv=16, S=2048, KS=2048,
+                  D=128, causal=False, window=-1, theta=None, kind="int8"),
     "4a": dict(workload="cfg4a_sliding_causal_w4096_s16384_rope", B=1, H=32, Hkv=8, S=16384, KS=16384, D=128,
                causal=True, window=4096, theta=1e6, kind="fp16"),
     "4b": dict(workload="cfg4b_two_sided_pm1024_s8192_rope", B=1, H=32, Hkv=8, S=8192, KS=8192, D=128,
@@ -413,6 +416,7 @@ def cpu_baseline(cfg, max_seconds=10.0):
     the whole workload."""
     from oracle import torch_oracle
 
+    torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
     B, H, Hkv, S, KS, D = 1, cfg["H"], cfg["Hkv"], cfg["S"], cfg["KS"], cfg["D"]
     G = H // Hkv
@@ -509,6 +513,51 @@ def measure_int8_peak():
                       "how": "torch._int_mm int8 8192^3 (2*N^3 OP): best of 10 launches; back to back for 4 s"}))
 
 
+def compare_cudnn():
+    """This library's FP16 kernel against cuDNN's SDPA (torch.nn.functional.
+    scaled_dot_product_attention restricted to the cuDNN backend) on the same box, same
+    tensors, no RoPE (cuDNN has no in-kernel RoPE): the Llama-3-8B GQA prefill shape
+    causal and not, and the MHA head_dim-64 shape of the INT8 workload."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    import rdnattention_b200 as R
+
+    def timed(fn, n=20, w=5):
+        for _ in range(w):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n
+
+    rows = []
+    for B, H, Hkv, S, D, causal in [(4, 32, 8, 4096, 128, True), (4, 32, 8, 4096, 128, False),
+                                    (8, 16, 16, 2048, 64, False)]:
+        g = torch.Generator(device="cuda").manual_seed(0)
+        q = torch.randn(B, H, S, D, generator=g, device="cuda", dtype=torch.float16)
+        k = torch.randn(B, Hkv, S, D, generator=g, device="cuda", dtype=torch.float16)
+        v = torch.randn(B, Hkv, S, D, generator=g, device="cuda", dtype=torch.float16)
+        fl = 4 * B * H * D * (S * (S + 1) / 2 if causal else S * S)
+        ours = timed(lambda: R.flash_attn(q, k, v, is_causal=causal))
+        row = {"shape": f"B{B} Hq{H} Hkv{Hkv} S{S} D{D} causal={causal}", "ours_ms": ours,
+               "ours_tflops": fl / ours / 1e9}
+        try:
+            with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+                cd = timed(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal, enable_gqa=Hkv != H))
+            row.update(cudnn_ms=cd, cudnn_tflops=fl / cd / 1e9, cudnn_over_ours=ours / cd)
+        except Exception as ex:  # the backend may be missing from a torch build
+            row["cudnn"] = f"unavailable: {type(ex).__name__}: {str(ex)[:120]}"
+        rows.append(row)
+    sampler_dev = torch.cuda.current_device()
+    print(json.dumps({"compare_cudnn": rows, "torch": torch.__version__,
+                      "gpu": torch.cuda.get_device_name(sampler_dev)}))
+
+
 def load_traffic(workload):
     """DRAM bytes per launch from a committed ncu summary (profiles/<kernel>_<workload>.txt)."""
     for f in (ROOT / "profiles").glob("*.txt"):
@@ -533,6 +582,7 @@ def run_reference(args, cfg, world):
     from oracle import torch_oracle
     from oracle.torch_oracle import flops
 
+    torch.set_num_threads(os.cpu_count() or 1)  # every host core (torchrun sets OMP_NUM_THREADS=1)
     metric, unit = metric_of(cfg)
     g = torch.Generator().manual_seed(0)
     S, KS, D, G = cfg["S"], cfg["KS"], cfg["D"], cfg["H"] // cfg["Hkv"]
@@ -595,9 +645,14 @@ def main():
                     help="N>1: pieces of the rank's units whose all-gathers overlap the next piece's kernel")
     ap.add_argument("--measure-int8-peak", action="store_true",
                     help="measure the INT8 tensor peak (torch._int_mm) and exit")
+    ap.add_argument("--compare-cudnn", action="store_true",
+                    help="time the FP16 kernel against cuDNN SDPA on the same shapes and exit")
     args = ap.parse_args()
     if args.measure_int8_peak:
         measure_int8_peak()
+        return
+    if args.compare_cudnn:
+        compare_cudnn()
         return
     cfg = dict(CONFIGS[args.config])
     if args.batch is not None:

@@ -63,9 +63,6 @@ namespace prefill {
 using namespace sm100;
 
 constexpr int BM = 128;  // query rows per tile (= TMEM lanes)
-#ifndef RDNA_EXP_TOKEN
-#define RDNA_EXP_TOKEN 1
-#endif
 
 struct Params {
     int B, H, Hkv, S, KS;
@@ -136,17 +133,7 @@ struct Traits {
     // Exp-phase token between the two softmax warpgroups, per scheduler: warp
     // w of one tile and warp w of the other (the pair that shares a MUFU) take
     // turns, without waiting for the other schedulers' warps.
-    static constexpr bool TOKEN = NT == 2 && RDNA_EXP_TOKEN;
-    // FP16 exponent phase on sm_100's paired fp32 instructions (scale-and-shift
-    // FMAs and row sums two at a time: fewer issues on the softmax critical path)
-#ifndef RDNA_F32X2
-#define RDNA_F32X2 1
-#endif
-    static constexpr bool F32X2 = RDNA_F32X2 != 0;
-#ifndef RDNA_I8_F32X2
-#define RDNA_I8_F32X2 1
-#endif
-    static constexpr bool I8X2 = I8 && RDNA_I8_F32X2 != 0;  // the same for the INT8 score conversion
+    static constexpr bool TOKEN = NT == 2;
     // Kernels that can rotate Q themselves (one item per CTA: the softmax
     // warps are idle until the first S, so they rotate the Q tile that the
     // first Q K^T waits for); the RoPE pre-pass then only rotates K.
@@ -647,26 +634,19 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
             // float(acc) * k_scale; the per-row q_scale * scale * log2(e) (rowscale) is
             // applied to the max and folded into the exponent's FMA below.
             const float* ksb = ksbuf + (gg & 1) * T::BC;
-            if constexpr (T::I8X2) {
-                // the bias subtraction (exact) and the key-scale product, two at a time
-                const uint64_t mb2 = f2(-12582912.0f, -12582912.0f);
-                if (kvec) {
+            // the bias subtraction (exact) and the key-scale product on sm_100's paired
+            // fp32 instructions, two at a time
+            const uint64_t mb2 = f2(-12582912.0f, -12582912.0f);
+            if (kvec) {
 #pragma unroll
-                    for (int c = 0; c < T::BC; c += 2) {
-                        const uint64_t v = fadd2(f2(i2f_biased(raw[c]), i2f_biased(raw[c + 1])), mb2);
-                        f2_split(fmul2(v, *reinterpret_cast<const uint64_t*>(ksb + c)), x[c], x[c + 1]);
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < T::BC; c += 2)
-                        f2_split(fadd2(f2(i2f_biased(raw[c]), i2f_biased(raw[c + 1])), mb2), x[c], x[c + 1]);
+                for (int c = 0; c < T::BC; c += 2) {
+                    const uint64_t v = fadd2(f2(i2f_biased(raw[c]), i2f_biased(raw[c + 1])), mb2);
+                    f2_split(fmul2(v, *reinterpret_cast<const uint64_t*>(ksb + c)), x[c], x[c + 1]);
                 }
-            } else if (kvec) {
-#pragma unroll
-                for (int c = 0; c < T::BC; ++c) x[c] = (i2f_biased(raw[c]) - 12582912.0f) * ksb[c];
             } else {
 #pragma unroll
-                for (int c = 0; c < T::BC; ++c) x[c] = i2f_biased(raw[c]) - 12582912.0f;
+                for (int c = 0; c < T::BC; c += 2)
+                    f2_split(fadd2(f2(i2f_biased(raw[c]), i2f_biased(raw[c + 1])), mb2), x[c], x[c + 1]);
             }
             if (!full) {
 #pragma unroll
@@ -755,12 +735,13 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         // one chunk of packed P is live at a time.  8 independent partial sums keep
         // the row-sum dependency chain short.
         float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if constexpr (!T::I8 && T::F32X2) {
+        if constexpr (!T::I8) {
             const float mul = (sl2 > 0.f) ? sl2 : 1.f;
             const uint64_t mul2 = f2(mul, mul), nm2 = f2(neg_m, neg_m);
             uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};  // (0.f, 0.f)
-            // all exponentials on the MUFU: moving a share to the FMA pipe
-            // (polynomial exp2) costs about as many issue slots as it saves MUFU time
+            // the scale-and-shift FMAs and row sums on sm_100's paired fp32 instructions
+            // (two per issue); all exponentials on the MUFU: moving a share to the FMA
+            // pipe (polynomial exp2) costs about as many issue slots as it saves
 #pragma unroll
             for (int c0 = 0; c0 < T::BC; c0 += 32) {
                 uint32_t pk[16];
@@ -777,22 +758,6 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
             }
 #pragma unroll
             for (int i = 0; i < 4; ++i) f2_split(ls2[i], ls[2 * i], ls[2 * i + 1]);
-        } else if constexpr (!T::I8) {
-            const float mul = (sl2 > 0.f) ? sl2 : 1.f;
-#pragma unroll
-            for (int c0 = 0; c0 < T::BC; c0 += 32) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int c = 0; c < 32; c += 2) {
-                    const float a0 = fmaf(x[c0 + c], mul, neg_m);
-                    const float a1 = fmaf(x[c0 + c + 1], mul, neg_m);
-                    const float p0 = ex2(a0);
-                    const float p1 = ex2(a1);
-                    ls[(c >> 1) & 7] += p0 + p1;
-                    pk[c / 2] = pack_half2(p0, p1);
-                }
-                tmem_st_x16(tS + c0 / 2, pk);
-            }
         } else {
             // p in [0, 1] against the running max, computed two at a time in half
             // precision (P only keeps 7 bits): fma(p, 127, 1024) in fp16 has unit
@@ -809,16 +774,9 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
 #pragma unroll
                 for (int c = 0; c < 32; c += 4) {
                     float a0, a1, a2, a3;
-                    if constexpr (T::I8X2) {
-                        const uint64_t ars2 = f2(ars, ars), nm2 = f2(neg_m, neg_m);
-                        f2_split(ffma2(f2(x[c0 + c], x[c0 + c + 1]), ars2, nm2), a0, a1);
-                        f2_split(ffma2(f2(x[c0 + c + 2], x[c0 + c + 3]), ars2, nm2), a2, a3);
-                    } else {
-                        a0 = fmaf(x[c0 + c], ars, neg_m);
-                        a1 = fmaf(x[c0 + c + 1], ars, neg_m);
-                        a2 = fmaf(x[c0 + c + 2], ars, neg_m);
-                        a3 = fmaf(x[c0 + c + 3], ars, neg_m);
-                    }
+                    const uint64_t ars2 = f2(ars, ars), nm2 = f2(neg_m, neg_m);
+                    f2_split(ffma2(f2(x[c0 + c], x[c0 + c + 1]), ars2, nm2), a0, a1);
+                    f2_split(ffma2(f2(x[c0 + c + 2], x[c0 + c + 3]), ars2, nm2), a2, a3);
                     const uint32_t e0 = ex2_h2(pack_half2(a0, a1));
                     const uint32_t e1 = ex2_h2(pack_half2(a2, a3));
                     hs[(c >> 2) & 7] = hadd2(hs[(c >> 2) & 7], hadd2(e0, e1));
@@ -993,6 +951,8 @@ __device__ void producer_q_role(const Params& p, const CUtensorMap* tmQ, uint8_t
     auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
     prefetch_tmap(tmQ);
     const uint64_t pol_q = policy_evict_first();
+    // Q comes from the RoPE pre-pass in the kernels that do not rotate it themselves
+    if constexpr (!T::ROPE_Q) grid_dependency_wait();
     int qfill = 0;
     for (int r = 0; r < 1; ++r) {
         const int item = item_at(p, r);
@@ -1020,6 +980,9 @@ __device__ void producer_kv_role(const Params& p, const CUtensorMap* tmK, const 
     prefetch_tmap(tmK);
     prefetch_tmap(tmV);
     const uint64_t pol_kv = policy_evict_last();
+    // K may be the RoPE pre-pass's output: a launch that overlaps the pre-pass
+    // (programmatic dependent launch) waits here for it; otherwise a no-op
+    grid_dependency_wait();
 
     int kfill[T::NSK] = {0};
     int vfill[T::NSV] = {0};

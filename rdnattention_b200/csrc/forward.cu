@@ -148,8 +148,11 @@ const char* check_common(const Common& c) {
 }
 
 // ---------------------------------------------------------------- launch
+// pdl: the launch may overlap the preceding kernel on the stream (the RoPE
+// pre-pass), whose output the kernel's producers wait for (griddepcontrol).
 template <class T>
-int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t stream, CUtensorMapDataType dt) {
+int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t stream, CUtensorMapDataType dt,
+                   bool pdl = false) {
     using namespace prefill;
     if (p.rope_q && !T::ROPE_Q) return fail(err, "internal: Q rotation requested from a kernel without it");
     CUtensorMap tmQ, tmK, tmV, tmO;
@@ -228,42 +231,49 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
             return fail(err, "internal: kernel register count does not match its register split");
     }
 
-    kern<<<static_cast<unsigned>(grid), T::THREADS, smem_bytes, stream>>>(tmQ, tmK, tmV, tmO, p);
-    ce = cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(T::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    ce = cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, tmO, p);
+    if (ce == cudaSuccess) ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
     return 0;
 }
 
-#ifndef RDNA_DUAL_MAX_D
-#define RDNA_DUAL_MAX_D 96
-#endif
 
 template <int D>
-int dispatch_f16_dim(char* err, const Common& c, const prefill::Params& p, cudaStream_t st) {
+int dispatch_f16_dim(char* err, const Common& c, const prefill::Params& p, cudaStream_t st, bool pdl) {
     using namespace prefill;
     constexpr CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if constexpr (D <= RDNA_DUAL_MAX_D) {
+    if constexpr (D <= 96) {
         // one 128-row tile per CTA, S double-buffered (256 TMEM columns), two
         // CTAs per SM: one CTA's prologue and epilogue overlap the other's main
         // loop.  Measured 6-9 % faster than the two-tile CTA for D <= 64 and
         // 5 % at D = 96 (three K/V stages); at D = 128 only two stages fit
         // beside a second CTA and it is 25 % slower.
         constexpr int st1 = D <= 64 ? 4 : 3;
-        return launch_prefill<Traits<D, D, 64, 1, st1, st1, false, true>>(err, c, p, st, dt);
+        return launch_prefill<Traits<D, D, 64, 1, st1, st1, false, true>>(err, c, p, st, dt, pdl);
     } else if constexpr (D <= 128) {
         // two 128-row tiles per CTA, 64-key blocks, S double-buffered in TMEM
         // (2 tiles x 2 buffers x 64 columns + 2 x D columns of O <= 512)
         constexpr int stages = D <= 64 ? 6 : D <= 96 ? 5 : 4;
-        return launch_prefill<Traits<D, D, 64, 2, stages, stages, false, true>>(err, c, p, st, dt);
+        return launch_prefill<Traits<D, D, 64, 2, stages, stages, false, true>>(err, c, p, st, dt, pdl);
     } else if constexpr (D <= 256) {
         // one tile per CTA (TMEM holds one O of up to 256 columns), 64-key blocks
         constexpr int stages = D <= 192 ? 3 : 2;
-        return launch_prefill<Traits<D, D, 64, 1, stages, stages, false>>(err, c, p, st, dt);
+        return launch_prefill<Traits<D, D, 64, 1, stages, stages, false>>(err, c, p, st, dt, pdl);
     } else {
         // head_dim > 256: two CTAs per tile, each owning half of the output columns
         constexpr int qk = 128 * D * 2, kt = 64 * D * 2, vt = 64 * 256 * 2;
         constexpr int stages = (2048 + qk + 2 * (kt + vt) <= 232448) ? 2 : 1;
-        return launch_prefill<Traits<D, 256, 64, 1, stages, stages, false>>(err, c, p, st, dt);
+        return launch_prefill<Traits<D, 256, 64, 1, stages, stages, false>>(err, c, p, st, dt, pdl);
     }
 }
 
@@ -359,7 +369,7 @@ int launch_rope(const ForwardParams& a, Common& c, void* ws, cudaStream_t st) {
     return 0;
 }
 
-int f16_attention(const ForwardParams& a, const Common& c, cudaStream_t st) {
+int f16_attention(const ForwardParams& a, const Common& c, cudaStream_t st, bool pdl) {
     prefill::Params p{};
     p.causal = a.causal ? 1 : 0;
     p.window = a.windowSize > 0 ? a.windowSize : 0;
@@ -369,7 +379,7 @@ int f16_attention(const ForwardParams& a, const Common& c, cudaStream_t st) {
     p.rope_sin = static_cast<const float*>(a.rot_sin);
     switch (a.headDim) {
 #define RDNA_D(Dv) \
-    case Dv: return dispatch_f16_dim<Dv>(g_err_f16, c, p, st);
+    case Dv: return dispatch_f16_dim<Dv>(g_err_f16, c, p, st, pdl);
         RDNA_D(32) RDNA_D(64) RDNA_D(96) RDNA_D(128) RDNA_D(160) RDNA_D(192) RDNA_D(224) RDNA_D(256)
         RDNA_D(288) RDNA_D(320) RDNA_D(352) RDNA_D(384) RDNA_D(416) RDNA_D(448) RDNA_D(480) RDNA_D(512)
 #undef RDNA_D
@@ -500,7 +510,8 @@ int forwardF16Ws(const ForwardParams& a, void* workspace, size_t workspace_bytes
             return fail(g_err_f16, "workspace must be 256-byte aligned");
         if (int rc = launch_rope(a, c, workspace, st)) return rc;
     }
-    return f16_attention(a, c, st);
+    // after a RoPE pre-pass the attention kernel is launched to overlap its tail
+    return f16_attention(a, c, st, need > 0);
 }
 
 int forwardF16(const ForwardParams& a, void* stream) {

@@ -59,27 +59,50 @@ struct Params {
 };
 
 // blockDim.x = rpb * cpr: thread -> (row within the block's slab, chunk).
-// Index math is per row and 32-bit (rows < 2^31).
+// Index math is per row and 32-bit (rows < 2^31).  Each thread handles two rows
+// per iteration with both loads issued before either store, so twice the bytes
+// are in flight per thread.  The first statement lets a dependent attention
+// kernel (launched with programmatic stream serialization) start its prologue
+// while this grid drains; that kernel waits for this grid's stores before it
+// reads the rotated rows.
+__device__ __forceinline__ const __half* rope_src(const Params& p, int row, int ch, int& which, unsigned& r,
+                                                 unsigned& s) {
+    which = row < p.rows[0] ? 0 : 1;
+    const Tensor4& T = p.t[which];
+    r = static_cast<unsigned>(which == 0 ? row : row - p.rows[0]);
+    s = r % static_cast<unsigned>(T.S);
+    const unsigned bh = r / static_cast<unsigned>(T.S);
+    const unsigned h = bh % static_cast<unsigned>(T.H);
+    const unsigned b = bh / static_cast<unsigned>(T.H);
+    return T.src + b * T.sb + h * T.sh + s * T.ss + ch * 8;
+}
+
+__device__ __forceinline__ void rope_store(const Params& p, int which, unsigned r, unsigned s, int ch,
+                                           const uint4& x) {
+    const int64_t toff = static_cast<int64_t>(s) * (p.D / 2) + ch * 4;
+    const float4 cv = __ldg(reinterpret_cast<const float4*>(p.cos_t + toff));
+    const float4 sv = __ldg(reinterpret_cast<const float4*>(p.sin_t + toff));
+    const uint4 y{rotate_pair(x.x, cv.x, sv.x), rotate_pair(x.y, cv.y, sv.y), rotate_pair(x.z, cv.z, sv.z),
+                  rotate_pair(x.w, cv.w, sv.w)};
+    *reinterpret_cast<uint4*>(p.t[which].dst + static_cast<int64_t>(r) * p.D + ch * 8) = y;
+}
+
 __global__ void __launch_bounds__(256) rope_rotate_kernel(const __grid_constant__ Params p) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int ch = threadIdx.x % p.cpr;
     const int rsub = threadIdx.x / p.cpr;
     if (rsub >= p.rpb) return;
-    const int total = p.rows[0] + p.rows[1];
-    for (int row = blockIdx.x * p.rpb + rsub; row < total; row += gridDim.x * p.rpb) {
-        const int which = row < p.rows[0] ? 0 : 1;
-        const Tensor4& T = p.t[which];
-        const unsigned r = static_cast<unsigned>(which == 0 ? row : row - p.rows[0]);
-        const unsigned s = r % static_cast<unsigned>(T.S);
-        const unsigned bh = r / static_cast<unsigned>(T.S);
-        const unsigned h = bh % static_cast<unsigned>(T.H);
-        const unsigned b = bh / static_cast<unsigned>(T.H);
-        const uint4 x = *reinterpret_cast<const uint4*>(T.src + b * T.sb + h * T.sh + s * T.ss + ch * 8);
-        const int64_t toff = static_cast<int64_t>(s) * (p.D / 2) + ch * 4;
-        const float4 cv = __ldg(reinterpret_cast<const float4*>(p.cos_t + toff));
-        const float4 sv = __ldg(reinterpret_cast<const float4*>(p.sin_t + toff));
-        const uint4 y{rotate_pair(x.x, cv.x, sv.x), rotate_pair(x.y, cv.y, sv.y), rotate_pair(x.z, cv.z, sv.z),
-                      rotate_pair(x.w, cv.w, sv.w)};
-        *reinterpret_cast<uint4*>(T.dst + static_cast<int64_t>(r) * p.D + ch * 8) = y;
+    const int64_t total = static_cast<int64_t>(p.rows[0]) + p.rows[1];
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * p.rpb;
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * p.rpb + rsub; row < total; row += 2 * stride) {
+        int w0, w1 = 0;
+        unsigned r0, s0, r1 = 0, s1 = 0;
+        const uint4 x0 = *reinterpret_cast<const uint4*>(rope_src(p, static_cast<int>(row), ch, w0, r0, s0));
+        const bool two = row + stride < total;
+        uint4 x1{0u, 0u, 0u, 0u};
+        if (two) x1 = *reinterpret_cast<const uint4*>(rope_src(p, static_cast<int>(row + stride), ch, w1, r1, s1));
+        rope_store(p, w0, r0, s0, ch, x0);
+        if (two) rope_store(p, w1, r1, s1, ch, x1);
     }
 }
 

@@ -138,6 +138,11 @@ RDNA_DEV void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Programmatic dependent launch: waits until the grids this one was launched to
+// overlap (cudaLaunchAttributeProgrammaticStreamSerialization) have completed and
+// their memory is visible.  Returns at once for an ordinary launch.
+RDNA_DEV void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ----------------------------------------------------------------------- TMA
 
 RDNA_DEV void prefetch_tmap(const CUtensorMap* m) {

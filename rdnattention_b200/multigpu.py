@@ -87,10 +87,27 @@ def pieces(shard: Shard, chunks: int):
     return out
 
 
-def _default_compute(q, k, v, **kw):
+def _default_compute(q, k, v, out=None, **kw):
     from . import flash_attn_strided
 
-    return flash_attn_strided(q, k, v, **kw)
+    return flash_attn_strided(q, k, v, out=out, **kw)
+
+
+def _uniform_axis(shards):
+    """"batch" or "kv_head" when the shards split one axis into equal consecutive ranges in
+    rank order (every rank's output then sits at offset rank * size of a contiguous block
+    of O, so the all-gather can run in place), else None."""
+    first = shards[0]
+    nb, ng = first.b1 - first.b0, first.g1 - first.g0
+    if nb == 0 or ng == 0:
+        return None
+    if all(s.g0 == first.g0 and s.g1 == first.g1 and s.b1 - s.b0 == nb and s.b0 == r * nb
+           for r, s in enumerate(shards)):
+        return "batch"
+    if all(s.b0 == first.b0 and s.b1 == first.b1 and s.g1 - s.g0 == ng and s.g0 == r * ng
+           for r, s in enumerate(shards)):
+        return "kv_head"
+    return None
 
 
 def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: int = -1, rot_cos=None,
@@ -100,11 +117,14 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     and receives the full output.  `compute` replaces the local kernel call
     (default: the sm_100a path through the C ABI).
 
-    chunks > 1 computes each rank's units in that many pieces along its shard axis
-    and starts each piece's all-gather (asynchronous, on the collective's own
-    stream) as soon as the piece is enqueued, so the transfer of piece c overlaps
-    the kernel of piece c + 1.  Every rank takes the same collective steps (pieces
-    that are empty on some ranks are padded)."""
+    When the plan splits one axis evenly (the usual case), each rank writes its
+    units straight into its block of the result and the all-gather runs in place;
+    `compute` is then called with an `out=` view to fill.  Otherwise, or with
+    chunks > 1 on a batch split, each rank computes its units in `chunks` pieces
+    along its shard axis and starts each piece's all-gather (asynchronous, on the
+    collective's own stream) as soon as the piece is enqueued, so the transfer of
+    piece c overlaps the kernel of piece c + 1; every rank takes the same
+    collective steps (pieces that are empty on some ranks are padded)."""
     if chunks < 1:
         raise ValueError("chunks must be >= 1")
     world = dist.get_world_size(group)
@@ -113,7 +133,30 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     Hkv = key.shape[1]
     G = H // Hkv
     compute = compute or _default_compute
-    per_rank = [pieces(plan(B, Hkv, world, r), chunks) for r in range(world)]
+    shards = [plan(B, Hkv, world, r) for r in range(world)]
+    axis = _uniform_axis(shards)
+    if axis is not None and (chunks == 1 or axis == "kv_head"):
+        # In place: the rank writes its units straight into its block of O and NCCL
+        # gathers the blocks around it (one collective for a batch split; one per batch
+        # element for a KV-head split, whose per-batch blocks [G*Hkv/world heads, S, D]
+        # are contiguous in rank order).  No staging buffers, no reassembly copy.
+        out = torch.empty(B, H, S, D, dtype=query.dtype, device=query.device)
+        me = shards[rank]
+        qs, ks, vs = local_views(query, key, value, me)
+        mine = out[me.b0:me.b1, me.g0 * G:me.g1 * G]
+        compute(qs, ks, vs, out=mine, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
+                rot_sin=rot_sin)
+        works = []
+        if axis == "batch":
+            works.append(dist.all_gather_into_tensor(out.view(-1), mine.reshape(-1), group=group, async_op=True))
+        else:
+            for b in range(B):
+                works.append(dist.all_gather_into_tensor(out[b].view(-1), out[b, me.g0 * G:me.g1 * G].reshape(-1),
+                                                         group=group, async_op=True))
+        for w in works:
+            w.wait()
+        return out
+    per_rank = [pieces(s, chunks) for s in shards]
 
     def elems(s: Shard):
         return (s.b1 - s.b0) * (s.g1 - s.g0) * G * S * D
