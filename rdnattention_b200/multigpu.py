@@ -19,12 +19,20 @@ import torch.distributed as dist
 
 @dataclass(frozen=True)
 class Shard:
-    """The rectangular block of units a rank owns: batches [b0, b1) x KV heads [g0, g1)."""
+    """The block of units a rank owns: batches b0, b0 + bstep, ... (< b1) x KV heads [g0, g1)."""
     axis: str  # "batch" or "kv_head"
     b0: int
     b1: int
     g0: int
     g1: int
+    bstep: int = 1
+
+    @property
+    def batches(self):
+        return range(self.b0, self.b1, self.bstep)
+
+    def units(self) -> int:
+        return len(self.batches) * (self.g1 - self.g0)
 
 
 def _split(n: int, world: int, rank: int):
@@ -34,15 +42,19 @@ def _split(n: int, world: int, rank: int):
 
 
 def plan(batch: int, kv_heads: int, world: int, rank: int) -> Shard:
-    """The rank's rectangle of (batch, KV-head) units.  Batch-major when every rank gets
-    whole batch elements (batch >= world), else KV-head groups when they cover the ranks
-    (kv_heads >= world); otherwise a grid of wb x wg ranks splits both axes, chosen to
-    keep the most ranks busy and then to balance the units per rank (B=2, Hkv=3 on 4
-    ranks: 2 x 2).  Uneven counts give the first ranks one more unit; ranks outside the
-    grid (fewer units than ranks) own nothing."""
+    """The rank's (batch, KV-head) units.  Batch-major when every rank gets whole batch
+    elements (batch >= world): round robin (rank r takes batches r, r + world, ...) when
+    they divide evenly, so that the c-th batch of every rank forms one contiguous block of
+    O in rank order, else consecutive ranges.  Otherwise KV-head groups when they cover
+    the ranks (kv_heads >= world); otherwise a grid of wb x wg ranks splits both axes,
+    chosen to keep the most ranks busy and then to balance the units per rank (B=2, Hkv=3
+    on 4 ranks: 2 x 2).  Uneven counts give the first ranks one more unit; ranks outside
+    the grid (fewer units than ranks) own nothing."""
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world of {world}")
     if batch >= world:
+        if batch % world == 0 and world > 1:
+            return Shard("batch", rank, batch, 0, kv_heads, bstep=world)
         b0, b1 = _split(batch, world, rank)
         return Shard("batch", b0, b1, 0, kv_heads)
     if kv_heads >= world:
@@ -67,9 +79,10 @@ def plan(batch: int, kv_heads: int, world: int, rank: int) -> Shard:
 def local_views(q, k, v, shard: Shard):
     """Strided views of the rank's units (no copies)."""
     G = q.shape[1] // k.shape[1]
-    qs = q[shard.b0:shard.b1, shard.g0 * G:shard.g1 * G]
-    ks = k[shard.b0:shard.b1, shard.g0:shard.g1]
-    vs = v[shard.b0:shard.b1, shard.g0:shard.g1]
+    b = slice(shard.b0, shard.b1, shard.bstep)
+    qs = q[b, shard.g0 * G:shard.g1 * G]
+    ks = k[b, shard.g0:shard.g1]
+    vs = v[b, shard.g0:shard.g1]
     return qs, ks, vs
 
 
@@ -79,8 +92,11 @@ def pieces(shard: Shard, chunks: int):
     out = []
     for c in range(chunks):
         if shard.axis == "batch":
-            lo, hi = _split(shard.b1 - shard.b0, chunks, c)
-            out.append(Shard("batch", shard.b0 + lo, shard.b0 + hi, shard.g0, shard.g1))
+            n = len(shard.batches)
+            lo, hi = _split(n, chunks, c)
+            b0 = shard.b0 + lo * shard.bstep
+            b1 = min(shard.b1, shard.b0 + hi * shard.bstep) if hi > lo else b0
+            out.append(Shard("batch", b0, b1, shard.g0, shard.g1, shard.bstep))
         else:
             lo, hi = _split(shard.g1 - shard.g0, chunks, c)
             out.append(Shard("kv_head", shard.b0, shard.b1, shard.g0 + lo, shard.g0 + hi))
@@ -94,17 +110,19 @@ def _default_compute(q, k, v, out=None, **kw):
 
 
 def _uniform_axis(shards):
-    """"batch" or "kv_head" when the shards split one axis into equal consecutive ranges in
-    rank order (every rank's output then sits at offset rank * size of a contiguous block
-    of O, so the all-gather can run in place), else None."""
+    """How the plan lets every all-gather run in place: "batch" when rank r owns batches
+    r, r + world, ... (so the c-th batch of every rank is one contiguous block of O in
+    rank order), "kv_head" when rank r owns the r-th equal range of KV heads of every
+    batch (each batch's block of O is contiguous in rank order); else None."""
+    world = len(shards)
     first = shards[0]
-    nb, ng = first.b1 - first.b0, first.g1 - first.g0
-    if nb == 0 or ng == 0:
+    if first.units() == 0:
         return None
-    if all(s.g0 == first.g0 and s.g1 == first.g1 and s.b1 - s.b0 == nb and s.b0 == r * nb
-           for r, s in enumerate(shards)):
+    if all(s.bstep == world and s.b0 == r and s.g0 == first.g0 and s.g1 == first.g1 and
+           len(s.batches) == len(first.batches) for r, s in enumerate(shards)):
         return "batch"
-    if all(s.b0 == first.b0 and s.b1 == first.b1 and s.g1 - s.g0 == ng and s.g0 == r * ng
+    ng = first.g1 - first.g0
+    if all(s.bstep == 1 and s.b0 == first.b0 and s.b1 == first.b1 and s.g1 - s.g0 == ng and s.g0 == r * ng
            for r, s in enumerate(shards)):
         return "kv_head"
     return None
@@ -118,13 +136,14 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     (default: the sm_100a path through the C ABI).
 
     When the plan splits one axis evenly (the usual case), each rank writes its
-    units straight into its block of the result and the all-gather runs in place;
-    `compute` is then called with an `out=` view to fill.  Otherwise, or with
-    chunks > 1 on a batch split, each rank computes its units in `chunks` pieces
-    along its shard axis and starts each piece's all-gather (asynchronous, on the
-    collective's own stream) as soon as the piece is enqueued, so the transfer of
-    piece c overlaps the kernel of piece c + 1; every rank takes the same
-    collective steps (pieces that are empty on some ranks are padded)."""
+    units straight into its block of the result and the all-gathers run in place
+    (`compute` is then called with an `out=` view to fill).  `chunks` > 1 computes
+    the rank's units in that many pieces (of batch elements) and starts each
+    piece's all-gathers (asynchronous, on the collective's own stream) as soon as
+    the piece is enqueued, so the transfer of piece c overlaps the kernel of piece
+    c + 1.  Uneven plans gather pieces into a staging buffer and copy them into
+    place; every rank takes the same collective steps (pieces that are empty on
+    some ranks are padded)."""
     if chunks < 1:
         raise ValueError("chunks must be >= 1")
     world = dist.get_world_size(group)
@@ -135,31 +154,44 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     compute = compute or _default_compute
     shards = [plan(B, Hkv, world, r) for r in range(world)]
     axis = _uniform_axis(shards)
-    if axis is not None and (chunks == 1 or axis == "kv_head"):
+    if axis is not None:
         # In place: the rank writes its units straight into its block of O and NCCL
-        # gathers the blocks around it (one collective for a batch split; one per batch
-        # element for a KV-head split, whose per-batch blocks [G*Hkv/world heads, S, D]
-        # are contiguous in rank order).  No staging buffers, no reassembly copy.
+        # gathers the blocks around it, one collective per batch element (the c-th
+        # batch of every rank for a round-robin batch split, the rank's KV heads of
+        # that batch for a KV-head split: contiguous in rank order either way), with no
+        # staging buffer and no reassembly copy.  The rank's units run in `chunks`
+        # pieces of batch elements; each piece's collectives (asynchronous, on NCCL's
+        # stream) overlap the next piece's kernel.
         out = torch.empty(B, H, S, D, dtype=query.dtype, device=query.device)
         me = shards[rank]
-        qs, ks, vs = local_views(query, key, value, me)
-        mine = out[me.b0:me.b1, me.g0 * G:me.g1 * G]
-        compute(qs, ks, vs, out=mine, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
-                rot_sin=rot_sin)
+        h0, h1 = me.g0 * G, me.g1 * G
+        nb = len(me.batches) if axis == "batch" else B
         works = []
-        if axis == "batch":
-            works.append(dist.all_gather_into_tensor(out.view(-1), mine.reshape(-1), group=group, async_op=True))
-        else:
-            for b in range(B):
-                works.append(dist.all_gather_into_tensor(out[b].view(-1), out[b, me.g0 * G:me.g1 * G].reshape(-1),
-                                                         group=group, async_op=True))
+        for c in range(min(chunks, nb)):
+            lo, hi = _split(nb, min(chunks, nb), c)
+            if axis == "batch":
+                piece = Shard("batch", me.b0 + lo * world, me.b0 + hi * world, me.g0, me.g1, world)
+            else:
+                piece = Shard("kv_head", lo, hi, me.g0, me.g1)
+            qs, ks, vs = local_views(query, key, value, piece)
+            mine = out[piece.b0:piece.b1:piece.bstep, h0:h1]
+            compute(qs, ks, vs, out=mine, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
+                    rot_sin=rot_sin)
+            for b in piece.batches:
+                if axis == "batch":
+                    whole = out[b - rank:b - rank + world]  # the c-th batch of every rank
+                    works.append(dist.all_gather_into_tensor(whole.reshape(-1), out[b].reshape(-1), group=group,
+                                                             async_op=True))
+                else:
+                    works.append(dist.all_gather_into_tensor(out[b].view(-1), out[b, h0:h1].reshape(-1),
+                                                             group=group, async_op=True))
         for w in works:
             w.wait()
         return out
     per_rank = [pieces(s, chunks) for s in shards]
 
     def elems(s: Shard):
-        return (s.b1 - s.b0) * (s.g1 - s.g0) * G * S * D
+        return s.units() * G * S * D
 
     gathered = []
     works = []
@@ -189,6 +221,6 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
             if sizes[r] == 0:
                 continue
             s = per_rank[r][c]
-            block = recv[r * cap:r * cap + sizes[r]].view(s.b1 - s.b0, (s.g1 - s.g0) * G, S, D)
-            out[s.b0:s.b1, s.g0 * G:s.g1 * G] = block
+            block = recv[r * cap:r * cap + sizes[r]].view(len(s.batches), (s.g1 - s.g0) * G, S, D)
+            out[s.b0:s.b1:s.bstep, s.g0 * G:s.g1 * G] = block
     return out

@@ -19,7 +19,7 @@ def test_plan_covers_every_unit_once(B, Hkv, world):
     seen = torch.zeros(B, Hkv, dtype=torch.int32)
     for r in range(world):
         s = plan(B, Hkv, world, r)
-        seen[s.b0:s.b1, s.g0:s.g1] += 1
+        seen[s.b0:s.b1:s.bstep, s.g0:s.g1] += 1
     assert torch.equal(seen, torch.ones_like(seen))
 
 
@@ -28,16 +28,19 @@ def test_plan_covers_every_unit_once(B, Hkv, world):
 def test_plan_keeps_ranks_busy(B, Hkv, world, busy):
     """Neither axis alone covering the ranks no longer idles them: both axes are split."""
     owned = [plan(B, Hkv, world, r) for r in range(world)]
-    assert sum((s.b1 - s.b0) * (s.g1 - s.g0) > 0 for s in owned) == busy
+    assert sum(s.units() > 0 for s in owned) == busy
 
 
 def test_local_views_are_strided_views():
     q = torch.randn(4, 8, 16, 64)
     k = torch.randn(4, 2, 16, 64)
-    s = plan(4, 2, 2, 1)
+    s = plan(4, 2, 2, 1)  # round robin: batches 1 and 3
     qs, ks, vs = local_views(q, k, k, s)
-    assert qs.data_ptr() == q[2:].data_ptr() and qs.stride() == q.stride()
+    assert qs.data_ptr() == q[1].data_ptr() and qs.stride(0) == 2 * q.stride(0) and qs.stride()[1:] == q.stride()[1:]
     assert ks.shape == (2, 2, 16, 64)
+    s = plan(3, 2, 2, 1)  # uneven: consecutive ranges
+    qs, _, _ = local_views(q[:3], k[:3], k[:3], s)
+    assert qs.data_ptr() == q[2].data_ptr() and qs.shape[0] == 1
 
 
 def _free_port():
@@ -92,7 +95,7 @@ def test_pieces_cover_each_shard_once(B, Hkv, world, chunks):
     seen = torch.zeros(B, Hkv, dtype=torch.int32)
     for r in range(world):
         for p in pieces(plan(B, Hkv, world, r), chunks):
-            seen[p.b0:p.b1, p.g0:p.g1] += 1
+            seen[p.b0:p.b1:p.bstep, p.g0:p.g1] += 1
     assert torch.equal(seen, torch.ones_like(seen))
 
 
@@ -114,3 +117,22 @@ def test_sharded_forward_overlapped_pieces(shape, causal, window, chunks):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert results == {0: True, 1: True}
+
+
+@pytest.mark.parametrize("shape,world,chunks", [
+    ((2, 8, 4, 9, 32), 4, 2),   # KV-head split (batch < ranks): per-batch in-place gathers, two pieces
+    ((8, 4, 2, 9, 32), 4, 2),   # round-robin batch split, two batches per rank, two pieces
+])
+def test_sharded_forward_in_place_on_four_ranks(shape, world, chunks):
+    """The in-place all-gathers with several ranks and pieces reassemble the full output."""
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, True, -1, queue, chunks)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert results == {r: True for r in range(world)}
