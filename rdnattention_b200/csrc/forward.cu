@@ -441,25 +441,23 @@ int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
     const int64_t units = static_cast<int64_t>(p.B) * p.Hkv;
     if (units > 65535) return fail(err, "too many (batch, kv head) units for one decode launch");
     const int64_t tiles = (static_cast<int64_t>(p.KS) + KT - 1) / KT;
-    // Cluster size: the smallest split (fewest CTAs, least combine work) whose
-    // waves over the SMs (one CTA each) are >= 95% full; each CTA keeps >= 8 tiles.
+    // Cluster size: the split with the least modelled time, waves over the SMs (one CTA
+    // each) x (tiles per CTA + a fixed cost per CTA that grows with the cluster: ring fill,
+    // DSMEM combine, and the SMs a wide cluster leaves idle while it waits for enough
+    // free SMs in one GPC).  The fixed costs are in tile times, fitted on B200 (32-key
+    // tiles, head_dim 128, KS 8192-32768, batch 8-64): clusters of 1 / 2 / 4 / 8 cost
+    // about 2 / 15 / 24 / 78 tiles.  Each CTA keeps >= 8 tiles.
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    auto wave_eff = [&](int c) {
-        const int64_t ctas = units * c;
-        const int64_t waves = (ctas + sms - 1) / sms;
-        return static_cast<double>(ctas) / static_cast<double>(waves * sms);
+    auto cost = [&](int c) {
+        const int64_t waves = (units * c + sms - 1) / sms;
+        const int64_t fixed = c == 1 ? 2 : c == 2 ? 15 : c == 4 ? 24 : 78;
+        return waves * ((tiles + c - 1) / c + fixed);
     };
     int cs = 1;
-    double best = wave_eff(1);
-    for (int c = 2; c <= MAX_CLUSTER && tiles / c >= 8; c *= 2) {
-        if (best >= 0.95) break;
-        if (wave_eff(c) > best + 1e-9) {
-            best = wave_eff(c);
-            cs = c;
-        }
-    }
+    for (int c = 2; c <= MAX_CLUSTER && tiles / c >= 8; c *= 2)
+        if (cost(c) < cost(cs)) cs = c;
 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(cs, static_cast<unsigned>(units), 1);
