@@ -641,8 +641,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--chunks", type=int, default=1,
-                    help="N>1: pieces of the rank's units whose all-gathers overlap the next piece's kernel")
+    ap.add_argument("--chunks", type=int, default=None,
+                    help="N>1: pieces of the rank's units whose all-gathers overlap the next piece's kernel "
+                         "(default: rdnattention_b200.multigpu.auto_chunks)")
     ap.add_argument("--measure-int8-peak", action="store_true",
                     help="measure the INT8 tensor peak (torch._int_mm) and exit")
     ap.add_argument("--compare-cudnn", action="store_true",
@@ -669,6 +670,9 @@ def main():
         return
 
     dist_on = world > 1
+    from rdnattention_b200.multigpu import auto_chunks
+
+    n_pieces = args.chunks or auto_chunks(cfg["B"], cfg["H"], cfg["S"], cfg["D"], world)
     torch.cuda.set_device(local)
     if dist_on:
         import datetime
@@ -697,7 +701,7 @@ def main():
     else:
         if cfg["kind"] == "int8":
             raise SystemExit("the sharded INT8 step is not wired into the bench (use --config 2/4a/4b/5)")
-        trip = [sharded_step_fns(cfg, xi, world, rank, args.chunks) for xi in xs]
+        trip = [sharded_step_fns(cfg, xi, world, rank, n_pieces) for xi in xs]
         shard = trip[0][2]
         turn = itertools.cycle([t[0] for t in trip])
         ms = time_device(lambda: next(turn)(), args.steps, args.warmup, dist_on, sampler)
@@ -763,14 +767,14 @@ def main():
         "config": config_dict(cfg, world, n_sets),
         "clocks": sampler.summary(),
         "e2e": e2e,
-        "gpu_launches": args.steps * launches_per_step(cfg) * (args.chunks if dist_on else 1),
+        "gpu_launches": args.steps * launches_per_step(cfg) * (n_pieces if dist_on else 1),
         "roofline": roof,
         "kernel_status": list(status),
     }
     if compute:
         line["compute_only"] = compute
-        line["step"] = ("flash_attn_sharded: the rank's units (one kernel per piece), then the NCCL "
-                        f"all-gather of O into every rank ({args.chunks} piece(s))")
+        line["step"] = ("flash_attn_sharded: the rank's units (one kernel per piece), each piece's NCCL "
+                        f"all-gather of O into every rank overlapping the next piece ({n_pieces} piece(s))")
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     print(json.dumps(line), flush=True)

@@ -128,8 +128,22 @@ def _uniform_axis(shards):
     return None
 
 
+# O bytes per batch element from which one piece (and one in-place all-gather) per batch
+# element pays: below it the collectives' fixed cost dominates (a decode step's O)
+AUTO_PIECE_BYTES = 4 << 20
+
+
+def auto_chunks(batch: int, heads: int, seq: int, head_dim: int, world: int, elem_bytes: int = 2) -> int:
+    """Pieces flash_attn_sharded uses with chunks=None: two when each rank holds at least
+    two batch elements' worth of a large O (so the first piece's all-gather overlaps the
+    second piece's kernel), else one."""
+    per_batch = heads * seq * head_dim * elem_bytes
+    local = batch // world if batch >= world else batch
+    return 2 if per_batch >= AUTO_PIECE_BYTES and local >= 2 else 1
+
+
 def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: int = -1, rot_cos=None,
-                       rot_sin=None, group=None, compute: Optional[Callable] = None, chunks: int = 1):
+                       rot_sin=None, group=None, compute: Optional[Callable] = None, chunks: Optional[int] = 1):
     """Forward attention over all ranks of `group`: every rank passes the same full
     [B, H, S, D] / [B, Hkv, KS, D] inputs, computes only its (batch, KV-head) units
     and receives the full output.  `compute` replaces the local kernel call
@@ -141,14 +155,19 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     the rank's units in that many pieces (of batch elements) and starts each
     piece's all-gathers (asynchronous, on the collective's own stream) as soon as
     the piece is enqueued, so the transfer of piece c overlaps the kernel of piece
-    c + 1.  Uneven plans gather pieces into a staging buffer and copy them into
-    place; every rank takes the same collective steps (pieces that are empty on
-    some ranks are padded)."""
-    if chunks < 1:
-        raise ValueError("chunks must be >= 1")
+    c + 1; a piece holding several batch elements of a round-robin batch split is
+    gathered through a staging buffer in one collective (cheap when O per batch
+    element is small, as in decode).  chunks=None picks the count from O's size
+    (auto_chunks).  Uneven plans gather pieces into a staging buffer and copy them
+    into place; every rank takes the same collective steps (pieces that are empty
+    on some ranks are padded)."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     B, H, S, D = query.shape
+    if chunks is None:
+        chunks = auto_chunks(B, H, S, D, world, query.element_size())
+    if chunks < 1:
+        raise ValueError("chunks must be >= 1")
     Hkv = key.shape[1]
     G = H // Hkv
     compute = compute or _default_compute
@@ -166,7 +185,7 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
         me = shards[rank]
         h0, h1 = me.g0 * G, me.g1 * G
         nb = len(me.batches) if axis == "batch" else B
-        works = []
+        works, staged = [], []
         for c in range(min(chunks, nb)):
             lo, hi = _split(nb, min(chunks, nb), c)
             if axis == "batch":
@@ -177,6 +196,16 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
             mine = out[piece.b0:piece.b1:piece.bstep, h0:h1]
             compute(qs, ks, vs, out=mine, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
                     rot_sin=rot_sin)
+            if axis == "batch" and len(piece.batches) > 1:
+                # several batch elements of every rank, interleaved in O: one staged
+                # collective (cheap when O per batch element is small, e.g. decode)
+                n = len(piece.batches)
+                recv = torch.empty((world, n) + tuple(mine.shape[1:]), dtype=out.dtype, device=out.device)
+                send = mine.contiguous()
+                works.append(dist.all_gather_into_tensor(recv.view(-1), send.view(-1), group=group, async_op=True))
+                c0 = piece.b0 - rank
+                staged.append((send, out[c0:c0 + n * world].view(n, world, *out.shape[1:]), recv))
+                continue
             for b in piece.batches:
                 if axis == "batch":
                     whole = out[b - rank:b - rank + world]  # the c-th batch of every rank
@@ -187,6 +216,8 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
                                                              group=group, async_op=True))
         for w in works:
             w.wait()
+        for _, dst, recv in staged:
+            dst.copy_(recv.transpose(0, 1))
         return out
     per_rank = [pieces(s, chunks) for s in shards]
 

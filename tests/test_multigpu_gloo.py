@@ -104,6 +104,8 @@ def test_pieces_cover_each_shard_once(B, Hkv, world, chunks):
     ((3, 4, 1, 9, 32), True, 4, 2),     # batch axis: rank 1's second piece is empty (padded send)
     ((1, 8, 4, 17, 32), False, 8, 3),   # KV-head axis, uneven pieces
     ((4, 8, 2, 24, 32), False, -1, 3),  # a piece empty on every rank (skipped by all)
+    ((8, 4, 2, 9, 32), True, -1, 2),    # round robin, two batch elements per piece: one staged collective each
+    ((8, 4, 2, 9, 32), False, -1, None),  # the automatic piece count
 ])
 def test_sharded_forward_overlapped_pieces(shape, causal, window, chunks):
     ctx = mp.get_context("spawn")
