@@ -383,9 +383,9 @@ def time_e2e_sharded(cfg, x, steps, warmup, world, rank):
     out_local = torch.empty(host["q"].shape, dtype=torch.float16, device="cuda")
     out_host = torch.empty(out_local.shape, dtype=torch.float16).pin_memory()
     G = cfg["H"] // cfg["Hkv"]
-    elems = (shard.b1 - shard.b0) * (shard.g1 - shard.g0) * G * cfg["S"] * cfg["D"]
+    elems = shard.units() * G * cfg["S"] * cfg["D"]
     units = [M.plan(cfg["B"], cfg["Hkv"], world, r) for r in range(world)]
-    cap = max((u.b1 - u.b0) * (u.g1 - u.g0) for u in units) * G * cfg["S"] * cfg["D"]
+    cap = max(u.units() for u in units) * G * cfg["S"] * cfg["D"]
     send = torch.zeros(cap, dtype=torch.float16, device="cuda")
     recv = torch.empty(world * cap, dtype=torch.float16, device="cuda")
     kw = dict(is_causal=cfg["causal"], window_size=cfg["window"]) if cfg["kind"] == "fp16" else {}
@@ -707,7 +707,7 @@ def main():
         ms = time_device(lambda: next(turn)(), args.steps, args.warmup, dist_on, sampler)
         cturn = itertools.cycle([t[1] for t in trip])
         c_ms = time_device(lambda: next(cturn)(), args.steps, args.warmup, dist_on)
-        units_rank = (shard.b1 - shard.b0) * (shard.g1 - shard.g0)
+        units_rank = shard.units()
         compute = {"what": "the rank's own units alone (no all-gather), max over ranks",
                    "ms_per_step": c_ms / args.steps,
                    "value": per_step_units * args.steps / (c_ms / 1e3) / scale,
