@@ -203,7 +203,7 @@ def sharded_step_fns(cfg, x, world, rank, chunks):
     kw = {}
     if cfg["kind"] == "fp16":
         kw = dict(is_causal=cfg["causal"], window_size=cfg["window"], rot_cos=x.get("cos"), rot_sin=x.get("sin"))
-    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank)
+    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank, interleave=chunks > 1)
     qs, ks, vs = M.local_views(x["q"], x["k"], x["v"], shard)
     out = torch.empty(qs.shape, dtype=torch.float16, device="cuda")
 
@@ -363,7 +363,7 @@ def time_e2e(cfg, x, steps, warmup, dist_on):
     return ms, h2d, d2h
 
 
-def time_e2e_sharded(cfg, x, steps, warmup, world, rank):
+def time_e2e_sharded(cfg, x, steps, warmup, world, rank, chunks=1):
     """N GPUs, end to end through the public API with host buffers: every step each
     rank copies its own units' Q/K/V (and the RoPE tables) in from pinned host
     memory, computes them, all-gathers O over NCCL (so every rank holds the whole
@@ -372,7 +372,7 @@ def time_e2e_sharded(cfg, x, steps, warmup, world, rank):
     import rdnattention_b200 as R
     from rdnattention_b200 import multigpu as M
 
-    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank)
+    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank, interleave=chunks > 1)
     qs, ks, vs = M.local_views(x["q"], x["k"], x["v"], shard)
     host = {"q": qs.contiguous().cpu().pin_memory(), "k": ks.contiguous().cpu().pin_memory(),
             "v": vs.contiguous().cpu().pin_memory()}
@@ -384,7 +384,7 @@ def time_e2e_sharded(cfg, x, steps, warmup, world, rank):
     out_host = torch.empty(out_local.shape, dtype=torch.float16).pin_memory()
     G = cfg["H"] // cfg["Hkv"]
     elems = shard.units() * G * cfg["S"] * cfg["D"]
-    units = [M.plan(cfg["B"], cfg["Hkv"], world, r) for r in range(world)]
+    units = [M.plan(cfg["B"], cfg["Hkv"], world, r, interleave=chunks > 1) for r in range(world)]
     cap = max(u.units() for u in units) * G * cfg["S"] * cfg["D"]
     send = torch.zeros(cap, dtype=torch.float16, device="cuda")
     recv = torch.empty(world * cap, dtype=torch.float16, device="cuda")
@@ -725,7 +725,7 @@ def main():
         if not dist_on:
             e2e_ms, h2d, d2h = time_e2e(cfg, x, e2e_steps, min(args.warmup, 3), dist_on)
         else:
-            e2e_ms, h2d, d2h = time_e2e_sharded(cfg, x, e2e_steps, min(args.warmup, 3), world, rank)
+            e2e_ms, h2d, d2h = time_e2e_sharded(cfg, x, e2e_steps, min(args.warmup, 3), world, rank, n_pieces)
         e2e_value = per_step_units * e2e_steps / (e2e_ms / 1e3) / scale
         e2e = {"value": e2e_value, "unit": metric_of(cfg)[1], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "steps": e2e_steps}

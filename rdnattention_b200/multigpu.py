@@ -41,11 +41,13 @@ def _split(n: int, world: int, rank: int):
     return start, start + base + (1 if rank < extra else 0)
 
 
-def plan(batch: int, kv_heads: int, world: int, rank: int) -> Shard:
+def plan(batch: int, kv_heads: int, world: int, rank: int, interleave: bool = True) -> Shard:
     """The rank's (batch, KV-head) units.  Batch-major when every rank gets whole batch
-    elements (batch >= world): round robin (rank r takes batches r, r + world, ...) when
-    they divide evenly, so that the c-th batch of every rank forms one contiguous block of
-    O in rank order, else consecutive ranges.  Otherwise KV-head groups when they cover
+    elements (batch >= world): with `interleave`, round robin (rank r takes batches r,
+    r + world, ...) when they divide evenly, so that the c-th batch of every rank forms
+    one contiguous block of O in rank order (a step in several pieces gathers each piece
+    in place); else consecutive ranges (rank r's block of O is contiguous and in rank
+    order, so a step in one piece gathers the whole O in place at once).  Otherwise KV-head groups when they cover
     the ranks (kv_heads >= world); otherwise a grid of wb x wg ranks splits both axes,
     chosen to keep the most ranks busy and then to balance the units per rank (B=2, Hkv=3
     on 4 ranks: 2 x 2).  Uneven counts give the first ranks one more unit; ranks outside
@@ -53,7 +55,7 @@ def plan(batch: int, kv_heads: int, world: int, rank: int) -> Shard:
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world of {world}")
     if batch >= world:
-        if batch % world == 0 and world > 1:
+        if interleave and batch % world == 0 and world > 1:
             return Shard("batch", rank, batch, 0, kv_heads, bstep=world)
         b0, b1 = _split(batch, world, rank)
         return Shard("batch", b0, b1, 0, kv_heads)
@@ -109,18 +111,23 @@ def _default_compute(q, k, v, out=None, **kw):
     return flash_attn_strided(q, k, v, out=out, **kw)
 
 
-def _uniform_axis(shards):
+def _uniform_axis(shards, kv_heads: int):
     """How the plan lets every all-gather run in place: "batch" when rank r owns batches
     r, r + world, ... (so the c-th batch of every rank is one contiguous block of O in
-    rank order), "kv_head" when rank r owns the r-th equal range of KV heads of every
-    batch (each batch's block of O is contiguous in rank order); else None."""
+    rank order), "batch_block" when rank r owns the r-th equal range of batches (its
+    block of O is contiguous and in rank order), "kv_head" when rank r owns the r-th
+    equal range of KV heads of every batch (each batch's block of O is contiguous in
+    rank order); else None."""
     world = len(shards)
     first = shards[0]
     if first.units() == 0:
         return None
-    if all(s.bstep == world and s.b0 == r and s.g0 == first.g0 and s.g1 == first.g1 and
-           len(s.batches) == len(first.batches) for r, s in enumerate(shards)):
+    whole_heads = all(s.g0 == 0 and s.g1 == kv_heads for s in shards)
+    nb = len(first.batches)
+    if whole_heads and all(s.bstep == world and s.b0 == r and len(s.batches) == nb for r, s in enumerate(shards)):
         return "batch"
+    if whole_heads and all(s.bstep == 1 and s.b0 == r * nb and s.b1 == (r + 1) * nb for r, s in enumerate(shards)):
+        return "batch_block"
     ng = first.g1 - first.g0
     if all(s.bstep == 1 and s.b0 == first.b0 and s.b1 == first.b1 and s.g1 - s.g0 == ng and s.g0 == r * ng
            for r, s in enumerate(shards)):
@@ -155,10 +162,10 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     the rank's units in that many pieces (of batch elements) and starts each
     piece's all-gathers (asynchronous, on the collective's own stream) as soon as
     the piece is enqueued, so the transfer of piece c overlaps the kernel of piece
-    c + 1; a piece holding several batch elements of a round-robin batch split is
-    gathered through a staging buffer in one collective (cheap when O per batch
-    element is small, as in decode).  chunks=None picks the count from O's size
-    (auto_chunks).  Uneven plans gather pieces into a staging buffer and copy them
+    c + 1 (a batch split is then round robin, and a piece holding several batch
+    elements of it is gathered through a staging buffer in one collective).  With
+    one piece a batch split takes consecutive ranges and a single in-place
+    all-gather.  chunks=None picks the count from O's size (auto_chunks).  Uneven plans gather pieces into a staging buffer and copy them
     into place; every rank takes the same collective steps (pieces that are empty
     on some ranks are padded)."""
     world = dist.get_world_size(group)
@@ -171,8 +178,19 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     Hkv = key.shape[1]
     G = H // Hkv
     compute = compute or _default_compute
-    shards = [plan(B, Hkv, world, r) for r in range(world)]
-    axis = _uniform_axis(shards)
+    shards = [plan(B, Hkv, world, r, interleave=chunks > 1) for r in range(world)]
+    axis = _uniform_axis(shards, Hkv)
+    if axis == "batch_block":
+        # One piece, consecutive batch ranges: the rank fills its contiguous block of O
+        # and one in-place all-gather assembles the rest around it.
+        out = torch.empty(B, H, S, D, dtype=query.dtype, device=query.device)
+        me = shards[rank]
+        qs, ks, vs = local_views(query, key, value, me)
+        mine = out[me.b0:me.b1]
+        compute(qs, ks, vs, out=mine, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
+                rot_sin=rot_sin)
+        dist.all_gather_into_tensor(out.view(-1), mine.view(-1), group=group)
+        return out
     if axis is not None:
         # In place: the rank writes its units straight into its block of O and NCCL
         # gathers the blocks around it, one collective per batch element (the c-th

@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from rdnattention_b200.multigpu import flash_attn_sharded, local_views, pieces, plan
+from rdnattention_b200.multigpu import _uniform_axis, flash_attn_sharded, local_views, pieces, plan
 
 
 @pytest.mark.parametrize("B,Hkv,world", [(4, 8, 2), (1, 8, 2), (3, 2, 2), (1, 1, 2), (8, 8, 8), (2, 3, 4), (5, 8, 8),
@@ -29,6 +29,21 @@ def test_plan_keeps_ranks_busy(B, Hkv, world, busy):
     """Neither axis alone covering the ranks no longer idles them: both axes are split."""
     owned = [plan(B, Hkv, world, r) for r in range(world)]
     assert sum(s.units() > 0 for s in owned) == busy
+
+
+@pytest.mark.parametrize("B,Hkv,world,interleave,axis", [
+    (8, 8, 2, True, "batch"), (8, 8, 2, False, "batch_block"), (8, 8, 4, False, "batch_block"),
+    (2, 8, 4, True, "kv_head"), (3, 2, 2, True, None), (2, 3, 4, True, None)])
+def test_in_place_gather_layouts(B, Hkv, world, interleave, axis):
+    """Which plans let the all-gathers write straight into O: interleaved batches (one
+    collective per piece), consecutive batch ranges (one collective for all of O) and
+    even KV-head ranges; uneven plans take the staged path."""
+    shards = [plan(B, Hkv, world, r, interleave=interleave) for r in range(world)]
+    assert _uniform_axis(shards, Hkv) == axis
+    seen = torch.zeros(B, Hkv, dtype=torch.int32)
+    for s in shards:
+        seen[s.b0:s.b1:s.bstep, s.g0:s.g1] += 1
+    assert torch.equal(seen, torch.ones_like(seen))
 
 
 def test_local_views_are_strided_views():
@@ -124,6 +139,7 @@ def test_sharded_forward_overlapped_pieces(shape, causal, window, chunks):
 @pytest.mark.parametrize("shape,world,chunks", [
     ((2, 8, 4, 9, 32), 4, 2),   # KV-head split (batch < ranks): per-batch in-place gathers, two pieces
     ((8, 4, 2, 9, 32), 4, 2),   # round-robin batch split, two batches per rank, two pieces
+    ((8, 4, 2, 9, 32), 4, 1),   # consecutive batch ranges, one piece: one in-place gather of all of O
 ])
 def test_sharded_forward_in_place_on_four_ranks(shape, world, chunks):
     """The in-place all-gathers with several ranks and pieces reassemble the full output."""
