@@ -191,23 +191,27 @@ def step_fn(cfg, x):
                                         out=out)
 
 
-def sharded_step_fns(cfg, x, world, rank, chunks):
+def sharded_step_fns(cfg, x, world, rank, chunks, sym=None):
     """The N-GPU step on one rank: (full, compute_only, shard).  `full` is the library
     call a user makes, rdnattention_b200.multigpu.flash_attn_sharded on the full
-    inputs (the rank's units, then the NCCL all-gather that gives every rank the
-    whole O, overlapped piece by piece when chunks > 1); `compute_only` launches
-    the same units' kernel alone."""
+    inputs: with `sym` (a SymmetricOutput) one kernel computes the rank's units and
+    stores every O tile into all ranks' outputs over NVLink, then a barrier kernel
+    (epoch flags over NVLink) orders those stores; else the rank's units, then the NCCL all-gather
+    that gives every rank the whole O (overlapped piece by piece when chunks > 1).
+    `compute_only` launches the same units' kernel alone."""
     import rdnattention_b200 as R
     from rdnattention_b200 import multigpu as M
 
     kw = {}
     if cfg["kind"] == "fp16":
         kw = dict(is_causal=cfg["causal"], window_size=cfg["window"], rot_cos=x.get("cos"), rot_sin=x.get("sin"))
-    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank, interleave=chunks > 1)
+    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank, interleave=sym is not None or chunks > 1)
     qs, ks, vs = M.local_views(x["q"], x["k"], x["v"], shard)
     out = torch.empty(qs.shape, dtype=torch.float16, device="cuda")
 
     def full():
+        if sym is not None:
+            return M.flash_attn_sharded(x["q"], x["k"], x["v"], out=sym, **kw)
         return M.flash_attn_sharded(x["q"], x["k"], x["v"], chunks=chunks, **kw)
 
     def compute_only():
@@ -232,13 +236,15 @@ def l2_note(cfg, n_sets, world=1):
             "each step's inputs were evicted by the steps before it, no flush")
 
 
-def config_dict(cfg, world, n_sets):
+def config_dict(cfg, world, n_sets, gather="fused"):
     """The workload description both arms print (the driver compares them)."""
+    how = ("O gathered into every rank by peer stores from the attention epilogue" if gather == "fused"
+           else "NCCL all-gather of O")
     return {"workload": cfg["workload"], "B": cfg["B"], "H": cfg["H"], "Hkv": cfg["Hkv"], "S": cfg["S"],
             "KS": cfg["KS"], "D": cfg["D"], "causal": cfg["causal"], "window": cfg["window"],
             "rope_theta": cfg["theta"], "global_batch": cfg["B"],
             "parallelism": ("one GPU" if world == 1 else
-                            f"(batch, kv-head group) units sharded over {world} ranks + NCCL all-gather of O"),
+                            f"(batch, kv-head group) units sharded over {world} ranks; {how}"),
             "l2": l2_note(cfg, n_sets, world)}
 
 
@@ -363,16 +369,17 @@ def time_e2e(cfg, x, steps, warmup, dist_on):
     return ms, h2d, d2h
 
 
-def time_e2e_sharded(cfg, x, steps, warmup, world, rank, chunks=1):
+def time_e2e_sharded(cfg, x, steps, warmup, world, rank, chunks=1, sym=None):
     """N GPUs, end to end through the public API with host buffers: every step each
     rank copies its own units' Q/K/V (and the RoPE tables) in from pinned host
-    memory, computes them, all-gathers O over NCCL (so every rank holds the whole
-    output) and copies its own units' output back to pinned host memory.  Events on
-    the current stream, max over ranks."""
+    memory, computes them, gathers O into every rank (with `sym`: the kernel's own
+    peer stores into every rank's SymmetricOutput plus the ordering barrier;
+    else an NCCL all-gather) and copies its own units' output back to pinned host
+    memory.  Events on the current stream, max over ranks."""
     import rdnattention_b200 as R
     from rdnattention_b200 import multigpu as M
 
-    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank, interleave=chunks > 1)
+    shard = M.plan(cfg["B"], cfg["Hkv"], world, rank, interleave=sym is not None or chunks > 1)
     qs, ks, vs = M.local_views(x["q"], x["k"], x["v"], shard)
     host = {"q": qs.contiguous().cpu().pin_memory(), "k": ks.contiguous().cpu().pin_memory(),
             "v": vs.contiguous().cpu().pin_memory()}
@@ -395,6 +402,15 @@ def time_e2e_sharded(cfg, x, steps, warmup, world, rank, chunks=1):
     def step():
         for n in host:
             dev[n].copy_(host[n], non_blocking=True)
+        if sym is not None:
+            dst, _ = sym.next_slot()
+            mine = dst[shard.b0:shard.b1:shard.bstep, shard.g0 * G:shard.g1 * G]
+            if qs.numel():
+                R.flash_attn_strided(dev["q"], dev["k"], dev["v"], out=mine, rot_cos=dev.get("cos"),
+                                     rot_sin=dev.get("sin"), peer_outputs=sym.peer_addresses(mine), **kw)
+            sym.order_stores()
+            out_host.copy_(mine, non_blocking=True)
+            return
         if qs.numel():
             R.flash_attn_strided(dev["q"], dev["k"], dev["v"], out=out_local, rot_cos=dev.get("cos"),
                                  rot_sin=dev.get("sin"), **kw)
@@ -618,7 +634,7 @@ def run_reference(args, cfg, world):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3 / max(args.steps, 1),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
-            "config": config_dict(cfg, world, input_sets(cfg, world)),
+            "config": config_dict(cfg, world, input_sets(cfg, world), args.gather),
             "sample_per_step": "one query head (fp32 torch oracle on the host cores)",
             "cpu_baseline": {"value": value, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
                              "sample": sample},
@@ -641,9 +657,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="N>1: how every rank receives O: peer stores from the kernels' epilogue into a "
+                         "SymmetricOutput (fused), or an NCCL all-gather after the kernel")
     ap.add_argument("--chunks", type=int, default=None,
-                    help="N>1: pieces of the rank's units whose all-gathers overlap the next piece's kernel "
-                         "(default: rdnattention_b200.multigpu.auto_chunks)")
+                    help="N>1 with --gather nccl: pieces of the rank's units whose all-gathers overlap the next "
+                         "piece's kernel (default: rdnattention_b200.multigpu.auto_chunks)")
     ap.add_argument("--measure-int8-peak", action="store_true",
                     help="measure the INT8 tensor peak (torch._int_mm) and exit")
     ap.add_argument("--compare-cudnn", action="store_true",
@@ -693,6 +712,7 @@ def main():
     per_step_units = work_units(cfg)
     scale = 1e9 if cfg["kind"] == "decode" else 1e12
     compute = None
+    sym = None
     if not dist_on:
         fns = [step_fn(cfg, xi) for xi in xs]
         turn = itertools.cycle(fns)
@@ -701,7 +721,12 @@ def main():
     else:
         if cfg["kind"] == "int8":
             raise SystemExit("the sharded INT8 step is not wired into the bench (use --config 2/4a/4b/5)")
-        trip = [sharded_step_fns(cfg, xi, world, rank, n_pieces) for xi in xs]
+        if args.gather == "fused":
+            from rdnattention_b200.multigpu import SymmetricOutput
+
+            sym = SymmetricOutput((cfg["B"], cfg["H"], cfg["S"], cfg["D"]))
+            n_pieces = 1
+        trip = [sharded_step_fns(cfg, xi, world, rank, n_pieces, sym) for xi in xs]
         shard = trip[0][2]
         turn = itertools.cycle([t[0] for t in trip])
         ms = time_device(lambda: next(turn)(), args.steps, args.warmup, dist_on, sampler)
@@ -725,11 +750,14 @@ def main():
         if not dist_on:
             e2e_ms, h2d, d2h = time_e2e(cfg, x, e2e_steps, min(args.warmup, 3), dist_on)
         else:
-            e2e_ms, h2d, d2h = time_e2e_sharded(cfg, x, e2e_steps, min(args.warmup, 3), world, rank, n_pieces)
+            e2e_ms, h2d, d2h = time_e2e_sharded(cfg, x, e2e_steps, min(args.warmup, 3), world, rank, n_pieces, sym)
         e2e_value = per_step_units * e2e_steps / (e2e_ms / 1e3) / scale
         e2e = {"value": e2e_value, "unit": metric_of(cfg)[1], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "steps": e2e_steps}
 
+    if sym is not None:
+        trip = None
+        sym.close()
     if rank != 0:
         if dist_on:
             torch.distributed.destroy_process_group()
@@ -764,17 +792,24 @@ def main():
         "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8" if cfg["kind"] == "int8" else "fp16", "data": "synthetic",
-        "config": config_dict(cfg, world, n_sets),
+        "config": config_dict(cfg, world, n_sets, args.gather),
         "clocks": sampler.summary(),
         "e2e": e2e,
-        "gpu_launches": args.steps * launches_per_step(cfg) * (n_pieces if dist_on else 1),
+        # (fused gather: the attention launch(es) plus the barrier kernel per step)
+        "gpu_launches": args.steps * (launches_per_step(cfg) * (n_pieces if dist_on else 1)
+                                      + (1 if dist_on and args.gather == "fused" else 0)),
         "roofline": roof,
         "kernel_status": list(status),
     }
     if compute:
         line["compute_only"] = compute
-        line["step"] = ("flash_attn_sharded: the rank's units (one kernel per piece), each piece's NCCL "
-                        f"all-gather of O into every rank overlapping the next piece ({n_pieces} piece(s))")
+        if args.gather == "fused":
+            line["step"] = ("flash_attn_sharded(out=SymmetricOutput): one launch per rank computes its units and "
+                            "stores every O tile into all ranks' outputs over NVLink (peer stores from the kernel "
+                            "epilogue), then a barrier kernel (epoch flags written over NVLink) orders the stores")
+        else:
+            line["step"] = ("flash_attn_sharded: the rank's units (one kernel per piece), each piece's NCCL "
+                            f"all-gather of O into every rank overlapping the next piece ({n_pieces} piece(s))")
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     print(json.dumps(line), flush=True)

@@ -112,4 +112,26 @@ int quantizeInt8QKV(const QuantizeInt8Params& params, void* stream);
 /// Whether a CUDA device is visible.
 bool hasDevice();
 
+/// Multi-GPU extensions.  forwardF16Ws / forwardInt8QK that also write the output
+/// to `n_peers` (<= 7) other GPUs' counterparts of params.o: same strides,
+/// mapped into this process (ipcOpen), 16-byte aligned.  The all-gather of the
+/// output is fused into the kernels' epilogues as NVLink peer stores; the peers
+/// may read them once this call's kernels have completed.
+int forwardF16WsPeers(const ForwardParams& params, void* workspace, size_t workspace_bytes, int n_peers,
+                      void* const* peers, void* stream);
+int forwardInt8QKPeers(const ForwardParamsInt8QK& params, int n_peers, void* const* peers, void* stream);
+/// Device memory another process can map: cudaMalloc plus its 64-byte IPC handle.
+int ipcAlloc(size_t bytes, void** ptr, void* handle);
+/// Maps another process's ipcAlloc memory into this one (peer access enabled).
+int ipcOpen(const void* handle, void** ptr);
+/// Unmaps ipcOpen memory.
+int ipcClose(void* ptr);
+/// Frees ipcAlloc memory (after every process that mapped it has closed it).
+int ipcFree(void* ptr);
+/// Enqueues the cross-GPU barrier of the fused all-gather on `stream`: writes
+/// `epoch` into slot `rank` of each other rank's flag array (peer_flags: the
+/// world - 1 other arrays in rank order, mapped here) and waits (bounded) until
+/// every other rank's slot of my_flags has reached it.
+int peerBarrier(int world, int rank, void* const* peer_flags, void* my_flags, unsigned int epoch, void* stream);
+
 }  // namespace rdna

@@ -213,8 +213,70 @@ RDNA_API int32_t rdna_debug_read_status(int32_t* out2);
  * wait_limit_ns: the wait for that tile expires, the CTA records the wait's
  * site in the status word (rdna_debug_read_status), unwinds (copies in flight
  * land, issued MMAs drain, TMEM is released) and skips its output store, so
- * that CTA's rows of O are left unwritten.  Nothing faults or hangs, and the
- * next call without the hook is unaffected.  Always returns 0. */
+ * that CTA's rows of O are left unwritten.  rdna_peer_barrier calls made by
+ * the thread meanwhile wait at most wait_limit_ns.  Nothing faults or hangs,
+ * and the next call without the hook is unaffected.  Always returns 0. */
 RDNA_API int32_t rdna_debug_set_wait_test(int32_t withhold_block, uint64_t wait_limit_ns);
+
+/* ---- Multi-GPU (extension, no counterpart in the single-device reference) ----
+ *
+ * The all-gather of the output across the GPUs of one node, fused into the
+ * kernels: a *_peers call also writes every output element to each of the
+ * n_peers (0..7) buffers in peer_outputs, the other GPUs' counterparts of
+ * `output` (same strides, mapped into this process with rdna_ipc_open,
+ * 16-byte aligned), with 16-byte stores over NVLink from the epilogue of each
+ * output tile, so the transfer overlaps the tiles still being computed.  The
+ * peers may read the values once this call's kernels have completed (order
+ * their reads after it, e.g. with a collective on the same stream). */
+
+/* rdna_attention_forward_ws with output replicas on other GPUs. */
+RDNA_API int32_t rdna_attention_forward_ws_peers(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* workspace, uint64_t workspace_bytes, int32_t n_peers, void* const* peer_outputs, void* stream);
+
+/* rdna_attention_forward_int8qk_vch with output replicas on other GPUs. */
+RDNA_API int32_t rdna_attention_forward_int8qk_vch_peers(
+    const void* q, const void* k, const void* v, void* output,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, float q_scale, float k_scale, float v_scale,
+    const void* q_scale_vec, const void* k_scale_vec, const void* v_channel,
+    int32_t causal, int32_t window_size,
+    int32_t n_peers, void* const* peer_outputs, void* stream);
+
+/* Device memory other processes can map (CUDA IPC): allocates `bytes` on the
+ * current device and writes its 64-byte handle to `handle`. */
+RDNA_API int32_t rdna_ipc_alloc(uint64_t bytes, void** ptr, void* handle);
+/* Maps another process's rdna_ipc_alloc memory (its 64-byte handle) into this
+ * process with peer access enabled. */
+RDNA_API int32_t rdna_ipc_open(const void* handle, void** ptr);
+/* Unmaps memory mapped by rdna_ipc_open. */
+RDNA_API int32_t rdna_ipc_close(void* ptr);
+/* Frees rdna_ipc_alloc memory; every process that mapped it must have closed
+ * it first. */
+RDNA_API int32_t rdna_ipc_free(void* ptr);
+
+/* Cross-GPU barrier ordering the peer stores of a *_peers call, enqueued on
+ * `stream` after it: writes `epoch` into word `rank` of each other rank's flag
+ * array (peer_flags: the world - 1 other arrays, in rank order without this
+ * rank, mapped into this process; 4-byte aligned) and waits until every other
+ * rank's word of my_flags (this rank's array, `world` words, zeroed before
+ * first use) has reached `epoch` (modulo 2^32).  Work queued after it sees
+ * every rank's stores.  Each wait is bounded (60 s); one that expires records
+ * code 0x401 in the status word (rdna_debug_read_status) and returns. */
+RDNA_API int32_t rdna_peer_barrier(int32_t world, int32_t rank, void* const* peer_flags, void* my_flags,
+                                   uint32_t epoch, void* stream);
 
 #endif /* RDNATTENTION_H_ */

@@ -90,6 +90,23 @@ def _lib_handle():
         lib.rdna_debug_read_status.restype = i32
         lib.rdna_debug_set_wait_test.argtypes = [i32, ctypes.c_uint64]
         lib.rdna_debug_set_wait_test.restype = i32
+        pp = ctypes.POINTER(vp)
+        lib.rdna_attention_forward_ws_peers.argtypes = ([vp] * 6 + [i64] * 12 + [u32] * 6 + [f32, i32, i32, i32]
+                                                        + [vp, ctypes.c_uint64, i32, pp, vp])
+        lib.rdna_attention_forward_ws_peers.restype = i32
+        lib.rdna_attention_forward_int8qk_vch_peers.argtypes = ([vp] * 4 + [i64] * 12 + [u32] * 6 + [f32] * 4
+                                                                + [vp, vp, vp] + [i32, i32, i32, pp, vp])
+        lib.rdna_attention_forward_int8qk_vch_peers.restype = i32
+        lib.rdna_ipc_alloc.argtypes = [ctypes.c_uint64, pp, vp]
+        lib.rdna_ipc_alloc.restype = i32
+        lib.rdna_ipc_open.argtypes = [vp, pp]
+        lib.rdna_ipc_open.restype = i32
+        lib.rdna_ipc_close.argtypes = [vp]
+        lib.rdna_ipc_close.restype = i32
+        lib.rdna_ipc_free.argtypes = [vp]
+        lib.rdna_ipc_free.restype = i32
+        lib.rdna_peer_barrier.argtypes = [i32, i32, pp, vp, u32, vp]
+        lib.rdna_peer_barrier.restype = i32
         _lib = lib
     return _lib
 
@@ -178,7 +195,63 @@ def _on_device(device):
     return torch.cuda.device(device)
 
 
-def _fp16_forward(query, key, value, is_causal, window_size, rot_cos, rot_sin, out, scale, require_contiguous):
+MAX_PEER_OUTPUTS = 7
+IPC_HANDLE_BYTES = 64
+
+
+def _peer_array(peer_outputs):
+    """(count, ctypes array) of peer output addresses, or (0, None)."""
+    if not peer_outputs:
+        return 0, None
+    addrs = [int(a) for a in peer_outputs]
+    if len(addrs) > MAX_PEER_OUTPUTS:
+        raise ValueError(f"at most {MAX_PEER_OUTPUTS} peer outputs, got {len(addrs)}")
+    return len(addrs), (ctypes.c_void_p * len(addrs))(*addrs)
+
+
+def _ipc_alloc(nbytes: int):
+    """Device memory on the current device that other processes can map:
+    (address, 64-byte CUDA IPC handle)."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    if _lib_handle().rdna_ipc_alloc(int(nbytes), ctypes.byref(ptr), handle) != 0:
+        raise RDNAttentionError(_last_error())
+    return ptr.value, handle.raw
+
+
+def _ipc_open(handle: bytes) -> int:
+    """Maps another process's _ipc_alloc memory (by its handle); returns its address here."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle has {IPC_HANDLE_BYTES} bytes, got {len(handle)}")
+    ptr = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    if _lib_handle().rdna_ipc_open(buf, ctypes.byref(ptr)) != 0:
+        raise RDNAttentionError(_last_error())
+    return ptr.value
+
+
+def _ipc_close(ptr: int) -> None:
+    if _lib_handle().rdna_ipc_close(ptr) != 0:
+        raise RDNAttentionError(_last_error())
+
+
+def _ipc_free(ptr: int) -> None:
+    if _lib_handle().rdna_ipc_free(ptr) != 0:
+        raise RDNAttentionError(_last_error())
+
+
+def _peer_barrier(world: int, rank: int, peer_flags, my_flags: int, epoch: int, device) -> None:
+    """Enqueues the cross-GPU barrier kernel (rdna_peer_barrier) on the current stream of `device`."""
+    arr = (ctypes.c_void_p * len(peer_flags))(*[int(a) for a in peer_flags])
+    with _on_device(device):
+        rc = _lib_handle().rdna_peer_barrier(world, rank, arr, my_flags, epoch & 0xFFFFFFFF,
+                                             _stream_handle(device))
+    if rc != 0:
+        raise RDNAttentionError(_last_error())
+
+
+def _fp16_forward(query, key, value, is_causal, window_size, rot_cos, rot_sin, out, scale, require_contiguous,
+                  peer_outputs=None):
     import torch
 
     _validate_inputs(query, key, value, torch.float16, require_contiguous)
@@ -198,13 +271,17 @@ def _fp16_forward(query, key, value, is_causal, window_size, rot_cos, rot_sin, o
     ws_bytes = lib.rdna_attention_forward_workspace_size(batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
                                                          has_rope)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=query.device) if ws_bytes else None
-    with _on_device(query.device):
-        rc = lib.rdna_attention_forward_ws(
-            query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(), cos_p, sin_p,
+    n_peers, peers = _peer_array(peer_outputs)
+    args = (query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(), cos_p, sin_p,
             qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
             batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
             float(scale), 1 if is_causal else 0, has_rope, int(window_size),
-            ws.data_ptr() if ws is not None else None, ws_bytes, _stream_handle(query.device))
+            ws.data_ptr() if ws is not None else None, ws_bytes)
+    with _on_device(query.device):
+        if n_peers:
+            rc = lib.rdna_attention_forward_ws_peers(*args, n_peers, peers, _stream_handle(query.device))
+        else:
+            rc = lib.rdna_attention_forward_ws(*args, _stream_handle(query.device))
     if rc != 0:
         raise RDNAttentionError(f"flash_attn failed: {_last_error()}")
     return out
@@ -227,18 +304,24 @@ def flash_attn(query, key, value, is_causal: bool = False, window_size: int = -1
 
 
 def flash_attn_strided(query, key, value, is_causal: bool = False, window_size: int = -1, rot_cos=None,
-                       rot_sin=None, out=None, scale=None):
+                       rot_sin=None, out=None, scale=None, peer_outputs=None):
     """flash_attn over arbitrary batch/head/seq strides (head_dim contiguous),
     e.g. a KV cache stored [batch, seq, kv_heads, head_dim] and viewed with
     ``.transpose(1, 2)``.  Optional preallocated ``out`` (any strides) and
     softmax ``scale``.  Extension: the reference reaches this only through
     its raw C ABI (tests/rope.py:9-27, tests/benchmark.py:232-263).
+
+    ``peer_outputs`` (multi-GPU extension): addresses of up to 7 other GPUs'
+    counterparts of ``out`` (same strides, mapped into this process, e.g. by
+    multigpu.SymmetricOutput); the kernels store every output tile there too,
+    over NVLink.  They hold the result once this call's kernels have completed.
     """
-    return _fp16_forward(query, key, value, is_causal, window_size, rot_cos, rot_sin, out, scale, False)
+    return _fp16_forward(query, key, value, is_causal, window_size, rot_cos, rot_sin, out, scale, False,
+                         peer_outputs)
 
 
 def flash_attn_int8qk(query, key, value, q_scale, k_scale, v_scale: float, is_causal: bool = False,
-                      window_size: int = -1):
+                      window_size: int = -1, *, out=None, peer_outputs=None):
     """INT8 attention, both GEMMs on the int8 tensor cores.  query/key/value:
     contiguous int8 [batch, heads, seq, head_dim], head_dim in
     SUPPORTED_HEAD_DIMS_INT8; output float16.  Symmetric dequant scales:
@@ -246,7 +329,10 @@ def flash_attn_int8qk(query, key, value, q_scale, k_scale, v_scale: float, is_ca
     (batch, heads, seq_len) / (batch, kv_heads, key_seq_len); v_scale is a
     float.  Causal, window, GQA and cross-attention supported; no RoPE.
 
-    Mirrors rdnattention/__init__.py:241-300 of the reference.
+    Mirrors rdnattention/__init__.py:241-300 of the reference.  Extensions
+    (keyword only): a preallocated float16 ``out`` (any strides), and
+    ``peer_outputs`` as in flash_attn_strided (other GPUs' counterparts of
+    ``out`` that the kernel also writes).
     """
     import torch
 
@@ -267,16 +353,24 @@ def flash_attn_int8qk(query, key, value, q_scale, k_scale, v_scale: float, is_ca
 
     q_scalar, q_vec = scale_arg(q_scale, "q_scale", (batch, heads, seq_len))
     k_scalar, k_vec = scale_arg(k_scale, "k_scale", (batch, kv_heads, key_seq_len))
-    out = torch.empty(query.shape, dtype=torch.float16, device=query.device)
+    if out is None:
+        out = torch.empty(query.shape, dtype=torch.float16, device=query.device)
+    elif out.dtype != torch.float16 or tuple(out.shape) != tuple(query.shape) or out.device != query.device:
+        raise RDNAttentionError("flash_attn_int8qk: out must be float16, shaped like query, on query's device")
     qs, ks, vs, os_ = query.stride(), key.stride(), value.stride(), out.stride()
-    with _on_device(query.device):
-        rc = _lib_handle().rdna_attention_forward_int8qk(
-            query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+    n_peers, peers = _peer_array(peer_outputs)
+    args = (query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
             qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
             batch, heads, kv_heads, seq_len, key_seq_len, head_dim,
             float(head_dim ** -0.5), q_scalar, k_scalar, float(v_scale),
-            q_vec.data_ptr() if q_vec is not None else None, k_vec.data_ptr() if k_vec is not None else None,
-            1 if is_causal else 0, int(window_size), _stream_handle(query.device))
+            q_vec.data_ptr() if q_vec is not None else None, k_vec.data_ptr() if k_vec is not None else None)
+    with _on_device(query.device):
+        if n_peers:
+            rc = _lib_handle().rdna_attention_forward_int8qk_vch_peers(
+                *args, None, 1 if is_causal else 0, int(window_size), n_peers, peers, _stream_handle(query.device))
+        else:
+            rc = _lib_handle().rdna_attention_forward_int8qk(*args, 1 if is_causal else 0, int(window_size),
+                                                             _stream_handle(query.device))
     if rc != 0:
         raise RDNAttentionError(f"flash_attn_int8qk failed: {_last_error()}")
     return out

@@ -134,6 +134,69 @@ RDNA_API int32_t rdna_attention_forward_ws(
     return 0;
 }
 
+RDNA_API int32_t rdna_attention_forward_ws_peers(
+    const void* q, const void* k, const void* v, void* output,
+    const void* rot_cos, const void* rot_sin,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, int32_t causal, int32_t has_rope, int32_t window_size,
+    void* workspace, uint64_t workspace_bytes, int32_t n_peers, void* const* peer_outputs, void* stream) {
+    const rdna::ForwardParams p = f16_params(q, k, v, output, rot_cos, rot_sin, q_stride_b, q_stride_h, q_stride_s,
+                                             k_stride_b, k_stride_h, k_stride_s, v_stride_b, v_stride_h, v_stride_s,
+                                             o_stride_b, o_stride_h, o_stride_s, batch_size, num_heads, num_kv_heads,
+                                             seq_len, key_seq_len, head_dim, scale, causal, has_rope, window_size);
+    if (rdna::forwardF16WsPeers(p, workspace, workspace_bytes, n_peers, peer_outputs, stream) != 0) {
+        set_error("Attention (fp16) failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API int32_t rdna_ipc_alloc(uint64_t bytes, void** ptr, void* handle) {
+    if (rdna::ipcAlloc(bytes, ptr, handle) != 0) {
+        set_error("IPC allocation failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API int32_t rdna_ipc_open(const void* handle, void** ptr) {
+    if (rdna::ipcOpen(handle, ptr) != 0) {
+        set_error("IPC open failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API int32_t rdna_ipc_close(void* ptr) {
+    if (rdna::ipcClose(ptr) != 0) {
+        set_error("IPC close failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API int32_t rdna_peer_barrier(int32_t world, int32_t rank, void* const* peer_flags, void* my_flags,
+                                   uint32_t epoch, void* stream) {
+    if (rdna::peerBarrier(world, rank, peer_flags, my_flags, epoch, stream) != 0) {
+        set_error("Peer barrier failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API int32_t rdna_ipc_free(void* ptr) {
+    if (rdna::ipcFree(ptr) != 0) {
+        set_error("IPC free failed: %s", rdna::lastError());
+        return -3;
+    }
+    return 0;
+}
+
 RDNA_API int32_t rdna_attention_forward_int8qk(
     const void* q, const void* k, const void* v, void* output,
     int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
@@ -232,7 +295,8 @@ RDNA_API int32_t rdna_debug_int8qk_scores(
     return 0;
 }
 
-RDNA_API int32_t rdna_attention_forward_int8qk_vch(
+// ForwardParamsInt8QK of the _vch entry points.
+static rdna::ForwardParamsInt8QK i8_params(
     const void* q, const void* k, const void* v, void* output,
     int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
     int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
@@ -242,7 +306,7 @@ RDNA_API int32_t rdna_attention_forward_int8qk_vch(
     uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
     float scale, float q_scale, float k_scale, float v_scale,
     const void* q_scale_vec, const void* k_scale_vec, const void* v_channel,
-    int32_t causal, int32_t window_size, void* stream) {
+    int32_t causal, int32_t window_size) {
     rdna::ForwardParamsInt8QK p{};
     p.q = q;
     p.k = k;
@@ -275,7 +339,50 @@ RDNA_API int32_t rdna_attention_forward_int8qk_vch(
     p.qScaleVec = q_scale_vec;
     p.kScaleVec = k_scale_vec;
     p.vChannel = v_channel;
+    return p;
+}
+
+RDNA_API int32_t rdna_attention_forward_int8qk_vch(
+    const void* q, const void* k, const void* v, void* output,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, float q_scale, float k_scale, float v_scale,
+    const void* q_scale_vec, const void* k_scale_vec, const void* v_channel,
+    int32_t causal, int32_t window_size, void* stream) {
+    const rdna::ForwardParamsInt8QK p =
+        i8_params(q, k, v, output, q_stride_b, q_stride_h, q_stride_s, k_stride_b, k_stride_h, k_stride_s,
+                  v_stride_b, v_stride_h, v_stride_s, o_stride_b, o_stride_h, o_stride_s, batch_size, num_heads,
+                  num_kv_heads, seq_len, key_seq_len, head_dim, scale, q_scale, k_scale, v_scale, q_scale_vec,
+                  k_scale_vec, v_channel, causal, window_size);
     if (rdna::forwardInt8QK(p, stream) != 0) {
+        set_error("Attention (int8qk) failed: %s", rdna::lastErrorInt8QK());
+        return -3;
+    }
+    return 0;
+}
+
+RDNA_API int32_t rdna_attention_forward_int8qk_vch_peers(
+    const void* q, const void* k, const void* v, void* output,
+    int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_s,
+    uint32_t batch_size, uint32_t num_heads, uint32_t num_kv_heads,
+    uint32_t seq_len, uint32_t key_seq_len, uint32_t head_dim,
+    float scale, float q_scale, float k_scale, float v_scale,
+    const void* q_scale_vec, const void* k_scale_vec, const void* v_channel,
+    int32_t causal, int32_t window_size,
+    int32_t n_peers, void* const* peer_outputs, void* stream) {
+    const rdna::ForwardParamsInt8QK p =
+        i8_params(q, k, v, output, q_stride_b, q_stride_h, q_stride_s, k_stride_b, k_stride_h, k_stride_s,
+                  v_stride_b, v_stride_h, v_stride_s, o_stride_b, o_stride_h, o_stride_s, batch_size, num_heads,
+                  num_kv_heads, seq_len, key_seq_len, head_dim, scale, q_scale, k_scale, v_scale, q_scale_vec,
+                  k_scale_vec, v_channel, causal, window_size);
+    if (rdna::forwardInt8QKPeers(p, n_peers, peer_outputs, stream) != 0) {
         set_error("Attention (int8qk) failed: %s", rdna::lastErrorInt8QK());
         return -3;
     }

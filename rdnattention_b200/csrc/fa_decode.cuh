@@ -78,6 +78,11 @@ struct Params {
     const float* rope_cos;
     const float* rope_sin;
     int kv_bcast;  // K/V axes broadcast with stride 0 (prefill::KV_BCAST_* bits): coordinate 0
+    // output replicas: n_peer other GPUs' counterparts of o (same strides, mapped
+    // into this process), each written with the same 16-byte chunks as o (no
+    // fence: the peers read them after this kernel has completed)
+    int n_peer;
+    __half* o_peer[7];
 };
 
 template <int D>
@@ -508,8 +513,13 @@ __global__ void __launch_bounds__(ROPE ? THREADS_ROPE : THREADS, 1) fa_decode_ke
             v.z = pack_half2(o[4] * inv, o[5] * inv);
             v.w = pack_half2(o[6] * inv, o[7] * inv);
             const int h = kvh * p.G + r / p.S, s = r % p.S;
-            if (!*abort_flag)
-                *reinterpret_cast<uint4*>(p.o + b * p.osb + h * p.osh + s * p.oss + 8 * c8) = v;
+            if (!*abort_flag) {
+                const int64_t off = b * p.osb + h * p.osh + s * p.oss + 8 * c8;
+                *reinterpret_cast<uint4*>(p.o + off) = v;
+#pragma unroll
+                for (int k = 0; k < 7; ++k)
+                    if (k < p.n_peer) *reinterpret_cast<uint4*>(p.o_peer[k] + off) = v;
+            }
         }
     }
     __syncwarp();

@@ -36,9 +36,15 @@
 //     for S itself.  An O rescale waits for PV(j-1) on its own barrier.
 //     With two tiles each tile has its own MMA issuer thread.
 //
-// RoPE is not applied here: rope.cuh rotates Q and K once per launch and the
-// kernel reads the rotated copies (rotating inside every CTA would repeat the
-// K rotation once per query tile that reads the block).
+// RoPE: rope.cuh rotates K once per launch and the kernel reads the rotated
+// copy (rotating inside every CTA would repeat the K rotation once per query
+// tile that reads the block); Q is rotated in shared memory by the softmax
+// warps (T::ROPE_Q kernels) or by the same pre-pass.
+//
+// Output replicas (Params::n_peer > 0, the multi-GPU all-gather fused into the
+// kernel): after the TMA store of a tile's O, the tile's softmax warps copy the
+// staged tile to the same place in each peer GPU's output with 16-byte stores
+// over NVLink, so the gather overlaps the CTAs still computing.
 //
 // TMEM columns: S(t, b) at [(t*NSB + b)*BC, +BC) (P aliases its first
 // columns); FP16: O_t (fp32) after all S.  INT8: ACC_t (s32 PV accumulator)
@@ -63,6 +69,7 @@ namespace prefill {
 using namespace sm100;
 
 constexpr int BM = 128;  // query rows per tile (= TMEM lanes)
+constexpr int kMaxPeers = 7;  // output replicas on other GPUs (8 GPUs of one node)
 
 struct Params {
     int B, H, Hkv, S, KS;
@@ -98,6 +105,11 @@ struct Params {
     // dbg_wait_limit_ns, so the wait for that tile expires and the CTA unwinds
     int dbg_withhold;
     unsigned long long dbg_wait_limit_ns;
+    // output replicas: n_peer other GPUs' counterparts of O (same strides, mapped
+    // into this process), written with the same values as O
+    int n_peer;
+    __half* o_peer[kMaxPeers];
+    int64_t o_sb, o_sh, o_ss;  // O element strides (batch, head, row)
 };
 
 constexpr int KV_BCAST_KB = 1, KV_BCAST_KH = 2, KV_BCAST_VB = 4, KV_BCAST_VH = 8;
@@ -415,6 +427,35 @@ template <int SW>
 __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
     const uint32_t off = static_cast<uint32_t>(row * SW + chunk * 16);
     return off ^ (((off >> 7) & (SW / 16 - 1)) << 4);
+}
+
+// Copies a tile's staged O (fp16 rows in swizzled boxes, `rows` valid rows of
+// `dv` columns from column dv0) to the same place in each peer's output: 16-byte
+// P2P stores, consecutive threads on consecutive chunks of a row (the rows of a
+// tile are contiguous in a [B, H, S, D] output, so a warp's stores cover 512
+// contiguous bytes).  No fence: the stores are complete when the kernel is, and
+// the peers read them only after that (a collective ordered after this kernel
+// on its stream), so the CTA exits while its stores still drain over NVLink.
+// Not inlined: its registers then do not add to the softmax role's allocation.
+template <class T>
+__device__ __noinline__ void store_peers(const Params& p, const uint8_t* stage, int b, int head, int row0,
+                                            int dv0, int dv, int r) {
+    const int cpr = dv / 8;  // 16-byte chunks per row
+    const int rows = min(BM, p.S - row0);
+    const int64_t base = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(head) * p.o_sh +
+                         static_cast<int64_t>(row0) * p.o_ss + dv0;
+#pragma unroll 1
+    for (int idx = r; idx < rows * cpr; idx += 4 * 32) {
+        const int row = idx / cpr, col = (idx % cpr) * 8;
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + (col / T::O_BOX) * T::O_BOX_BYTES +
+                                                        swz_off<T::O_SW>(row, (col % T::O_BOX) / 8));
+        const int64_t off = base + static_cast<int64_t>(row) * p.o_ss + col;
+        // constant indices: the pointers stay in the parameter bank (a runtime index
+        // would copy the array to local memory)
+#pragma unroll
+        for (int k = 0; k < kMaxPeers; ++k)
+            if (k < p.n_peer) *reinterpret_cast<uint4*>(p.o_peer[k] + off) = v;
+    }
 }
 
 // --------------------------------------------------------------- softmax
@@ -920,6 +961,10 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         if (lane == 0) mbar_arrive(bar(Bars::O_EMPTY + t));
     }
     mbar_arrive(bar(Bars::EPI + t));
+    if constexpr (!T::DUMP_S) {  // (debug score dumps take no output replicas)
+        if (p.n_peer > 0 && !aborted && warp_wait(bar(Bars::EPI + t), n_st & 1, ab, SITE_SM_EPI) && !*ab.flag)
+            store_peers<T>(p, stage, w.b, w.head[t], row0, dv0, dv, r);
+    }
     if (r == 0) {
         if (!aborted && mbar_wait(bar(Bars::EPI + t), n_st & 1, ab, SITE_SM_EPI) && !*ab.flag) {
             const int nbox = dv / T::O_BOX;
@@ -1521,6 +1566,10 @@ __device__ void softmax_role_i8x2(const Params& p, const CUtensorMap* tmO, int t
         fence_proxy_async_smem();
     }
     mbar_arrive(bar(Bars::EPI + t));
+    if constexpr (!T::DUMP_S) {  // (debug score dumps take no output replicas)
+        if (p.n_peer > 0 && !aborted && warp_wait(bar(Bars::EPI + t), 0, ab, SITE_SM_EPI) && !*ab.flag)
+            store_peers<T>(p, stage, w.b, w.head[t], row0, dv0, dv, r);
+    }
     if (r == 0) {
         if (!aborted && mbar_wait(bar(Bars::EPI + t), 0, ab, SITE_SM_EPI) && !*ab.flag) {
             const int nbox = dv / T::O_BOX;

@@ -19,6 +19,7 @@
 
 #include "fa_decode.cuh"
 #include "fa_prefill.cuh"
+#include "peer.cuh"
 #include "rope.cuh"
 #include "quant.cuh"
 
@@ -110,6 +111,33 @@ uint64_t bc_extent(uint64_t n, bool bcast) { return bcast ? 1u : n; }
 thread_local int g_dbg_withhold = -1;
 thread_local unsigned long long g_dbg_wait_limit_ns = 0;
 
+// Output replicas of the call in progress on this thread (the *Peers entry
+// points set them for the duration of one call): other GPUs' counterparts of
+// the output pointer, which every kernel writes with the same values as O.
+struct OutputPeers {
+    int n = 0;
+    void* o[prefill::kMaxPeers] = {};
+};
+thread_local OutputPeers g_peers;
+
+// Sets g_peers for one call and clears it when the call returns.
+struct PeerScope {
+    PeerScope(int n, void* const* o) {
+        g_peers.n = n;
+        for (int i = 0; i < n; ++i) g_peers.o[i] = o[i];
+    }
+    ~PeerScope() { g_peers = OutputPeers{}; }
+};
+
+const char* check_peers(int n, void* const* o) {
+    if (n < 0 || n > prefill::kMaxPeers) return "peer output count must be between 0 and 7";
+    if (n > 0 && o == nullptr) return "null peer output array";
+    for (int i = 0; i < n; ++i)
+        if (o[i] == nullptr || (reinterpret_cast<uintptr_t>(o[i]) & 15u) != 0)
+            return "peer outputs must be non-null and 16-byte aligned";
+    return nullptr;
+}
+
 const char* check_common(const Common& c) {
     // with key_seq_len == 0 K and V are never read (an empty tensor may have a null pointer)
     if (c.q == nullptr || c.o == nullptr || (c.KS > 0 && (c.k == nullptr || c.v == nullptr)))
@@ -173,6 +201,11 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
                    {c.vs[2], c.vs[1], c.vs[0]}};
     p.dbg_withhold = g_dbg_withhold;
     p.dbg_wait_limit_ns = g_dbg_wait_limit_ns;
+    p.n_peer = g_peers.n;
+    for (int i = 0; i < g_peers.n; ++i) p.o_peer[i] = static_cast<__half*>(g_peers.o[i]);
+    p.o_sb = c.os[0];
+    p.o_sh = c.os[1];
+    p.o_ss = c.os[2];
     const View4 vo{c.o, {c.D, c.S, c.H, c.B}, {c.os[2], c.os[1], c.os[0]}};
     const char* e = nullptr;
     if ((e = make_map(&tmQ, vq, dt, T::ESZ, T::BOX, BM, sw)) ||
@@ -419,6 +452,8 @@ int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
     p.rope = a.hasRope ? 1 : 0;
     p.rope_cos = static_cast<const float*>(a.rot_cos);
     p.rope_sin = static_cast<const float*>(a.rot_sin);
+    p.n_peer = g_peers.n;
+    for (int i = 0; i < g_peers.n; ++i) p.o_peer[i] = static_cast<__half*>(g_peers.o[i]);
 
     CUtensorMap tmK, tmV;
     const bool nokv = a.keySeqLen == 0;
@@ -637,6 +672,80 @@ int int8_forward(const ForwardParamsInt8QK& a, int32_t* s_dump, void* stream) {
 }  // namespace
 
 int forwardInt8QK(const ForwardParamsInt8QK& a, void* stream) { return int8_forward(a, nullptr, stream); }
+
+int forwardF16WsPeers(const ForwardParams& a, void* workspace, size_t workspace_bytes, int n_peers,
+                      void* const* peers, void* stream) {
+    if (const char* e = check_peers(n_peers, peers)) return fail(g_err_f16, "%s", e);
+    PeerScope scope(n_peers, peers);
+    return forwardF16Ws(a, workspace, workspace_bytes, stream);
+}
+
+int forwardInt8QKPeers(const ForwardParamsInt8QK& a, int n_peers, void* const* peers, void* stream) {
+    if (const char* e = check_peers(n_peers, peers)) return fail(g_err_i8, "%s", e);
+    PeerScope scope(n_peers, peers);
+    return int8_forward(a, nullptr, stream);
+}
+
+// ------------------------------------------------ device memory shared across processes
+int ipcAlloc(size_t bytes, void** ptr, void* handle) {
+    if (ptr == nullptr || handle == nullptr) return fail(g_err_f16, "null argument");
+    if (bytes == 0) return fail(g_err_f16, "empty allocation");
+    *ptr = nullptr;
+    cudaError_t ce = cudaMalloc(ptr, bytes);
+    if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    cudaIpcMemHandle_t h{};
+    ce = cudaIpcGetMemHandle(&h, *ptr);
+    if (ce != cudaSuccess) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    return 0;
+}
+
+int ipcOpen(const void* handle, void** ptr) {
+    if (ptr == nullptr || handle == nullptr) return fail(g_err_f16, "null argument");
+    cudaIpcMemHandle_t h{};
+    std::memcpy(&h, handle, sizeof(h));
+    cudaError_t ce = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    return 0;
+}
+
+int ipcClose(void* ptr) {
+    cudaError_t ce = cudaIpcCloseMemHandle(ptr);
+    if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    return 0;
+}
+
+int peerBarrier(int world, int rank, void* const* peer_flags, void* my_flags, unsigned int epoch, void* stream) {
+    if (world < 2 || world > peer::kMaxPeers + 1 || rank < 0 || rank >= world)
+        return fail(g_err_f16, "barrier: world must be 2 to 8 ranks and 0 <= rank < world");
+    auto bad = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 3u) != 0; };
+    if (peer_flags == nullptr || bad(my_flags)) return fail(g_err_f16, "barrier: null or misaligned flag array");
+    peer::BarrierParams p{};
+    for (int i = 0; i < world - 1; ++i) {
+        if (bad(peer_flags[i])) return fail(g_err_f16, "barrier: null or misaligned flag array");
+        p.peer_flags[i] = static_cast<unsigned int*>(peer_flags[i]);
+    }
+    p.world = world;
+    p.rank = rank;
+    p.my_flags = static_cast<unsigned int*>(my_flags);
+    p.epoch = epoch;
+    // (the expired-wait test hook shortens the barrier's waits too)
+    p.limit_ns = g_dbg_wait_limit_ns > 0 ? g_dbg_wait_limit_ns : peer::kBarrierLimitNs;
+    peer::barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    cudaError_t ce = cudaGetLastError();
+    if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    return 0;
+}
+
+int ipcFree(void* ptr) {
+    cudaError_t ce = cudaFree(ptr);
+    if (ce != cudaSuccess) return fail(g_err_f16, "%s", cudaGetErrorString(ce));
+    return 0;
+}
 
 int debugInt8QKScores(const ForwardParamsInt8QK& a, void* scores, void* stream) {
     if (scores == nullptr || (reinterpret_cast<uintptr_t>(scores) & 3u) != 0)

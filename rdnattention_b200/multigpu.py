@@ -2,10 +2,20 @@
 
 The units of work — a batch element together with one KV head and the G
 query heads that read it — are independent, so each rank computes its own
-units with no inter-GPU traffic inside the kernel, and one collective
-all-gather assembles the full output O on every rank (NCCL over NVLink on
-the GPU path).  Shards are strided views of the full tensors (base-pointer
-offsets, original strides), so nothing is repacked.
+units and every rank receives the full output O.  Two ways to assemble O:
+
+* fused (``out=SymmetricOutput(...)``): every rank's output buffer is mapped
+  into every other rank's process (CUDA IPC), and the attention kernels store
+  each finished O tile into all ranks' buffers over NVLink from their
+  epilogue, so the gather overlaps the tiles still being computed; a small
+  barrier kernel (epoch flags written over NVLink) then orders the peers'
+  stores before anything that reads O;
+* NCCL: the rank's units are computed into its block of O and NCCL
+  all-gathers the blocks (in place when the plan allows, in pieces that
+  overlap the next piece's kernel).
+
+Shards are strided views of the full tensors (base-pointer offsets, original
+strides), so nothing is repacked.
 
 The reference library is single-device; this module is the multi-GPU layer
 the B200 build adds around its C ABI.
@@ -105,10 +115,10 @@ def pieces(shard: Shard, chunks: int):
     return out
 
 
-def _default_compute(q, k, v, out=None, **kw):
+def _default_compute(q, k, v, out=None, peer_outputs=None, **kw):
     from . import flash_attn_strided
 
-    return flash_attn_strided(q, k, v, out=out, **kw)
+    return flash_attn_strided(q, k, v, out=out, peer_outputs=peer_outputs, **kw)
 
 
 def _uniform_axis(shards, kv_heads: int):
@@ -149,8 +159,115 @@ def auto_chunks(batch: int, heads: int, seq: int, head_dim: int, world: int, ele
     return 2 if per_batch >= AUTO_PIECE_BYTES and local >= 2 else 1
 
 
+class _DeviceArray:
+    """A raw device allocation seen through __cuda_array_interface__ (torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class SymmetricOutput:
+    """Output buffers of one shape on every rank of `group`, each mapped into
+    every other rank's process (CUDA IPC), for flash_attn_sharded(out=...): the
+    kernels store each O tile into every rank's copy over NVLink, the
+    all-gather fused into the attention epilogue.
+
+    Collective: every rank constructs it with the same shape (on its current
+    CUDA device) and calls close() together.  `slots` buffers are used in turn,
+    one per call: the tensor a call returns holds the result until this rank
+    makes its next call with this object (consume or copy it, on the current
+    stream, before then); other ranks' next kernels only write the following
+    slot."""
+
+    def __init__(self, shape, dtype=torch.float16, group=None, slots: int = 2):
+        import rdnattention_b200 as R
+
+        if dtype != torch.float16:
+            raise ValueError("the fused gather writes float16 outputs")
+        if slots < 2:
+            raise ValueError("slots must be >= 2 (a rank's next kernel writes the other slot)")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world - 1 > R.MAX_PEER_OUTPUTS:
+            raise ValueError(f"at most {R.MAX_PEER_OUTPUTS + 1} ranks")
+        self.shape = tuple(int(x) for x in shape)
+        self.dtype = dtype
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        n = 1
+        for x in self.shape:
+            n *= x
+        self.slot_bytes = (n * 2 + 255) // 256 * 256
+        flags_off = self.slot_bytes * slots  # then one flag word per rank (the barrier's epochs)
+        with torch.cuda.device(self.device):
+            self._base, handle = R._ipc_alloc(flags_off + 256)
+        self._flags = torch.as_tensor(_DeviceArray(self._base + flags_off, (self.world,), "<i4"), device=self.device)
+        self._flags.zero_()  # before the handles go out: no peer signals before it has them
+        self._epoch = 0
+        mine = torch.frombuffer(bytearray(handle), dtype=torch.uint8).to(self.device)
+        every = torch.empty(self.world * R.IPC_HANDLE_BYTES, dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().numpy().tobytes()
+        self._peer_bases = []  # the other ranks' allocations, in rank order
+        with torch.cuda.device(self.device):
+            for r in range(self.world):
+                if r != self.rank:
+                    h = every[r * R.IPC_HANDLE_BYTES:(r + 1) * R.IPC_HANDLE_BYTES]
+                    self._peer_bases.append(R._ipc_open(h))
+        self._peer_flags = [b + flags_off for b in self._peer_bases]
+        self.slots = [torch.as_tensor(_DeviceArray(self._base + i * self.slot_bytes, self.shape, "<f2"),
+                                      device=self.device) for i in range(slots)]
+        self._turn = 0
+
+    def next_slot(self):
+        """The slot the next call writes, and its offset in every allocation."""
+        i = self._turn
+        self._turn = (self._turn + 1) % len(self.slots)
+        return self.slots[i], i * self.slot_bytes
+
+    def peer_addresses(self, view) -> list:
+        """Addresses, in the other ranks' buffers, of the elements `view` (a view of
+        one of this rank's slots) covers here."""
+        off = view.data_ptr() - self._base
+        if not 0 <= off < self.slot_bytes * len(self.slots):
+            raise ValueError("view is not inside this SymmetricOutput")
+        return [b + off for b in self._peer_bases]
+
+    def order_stores(self):
+        """Stream-ordered barrier (a one-block kernel over peer flag words): work
+        queued after it on the current stream runs once every rank's kernels
+        before it (and their peer stores) have completed.  Every rank calls it
+        once per call of the fused path, in the same order."""
+        import rdnattention_b200 as R
+
+        self._epoch += 1
+        R._peer_barrier(self.world, self.rank, self._peer_flags, self._flags.data_ptr(), self._epoch, self.device)
+
+    def close(self):
+        """Collective: unmaps the peers' buffers and frees this rank's."""
+        import rdnattention_b200 as R
+
+        if self._base is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for b in self._peer_bases:
+                R._ipc_close(b)
+        self._peer_bases = []
+        self._peer_flags = []
+        self.slots = []
+        self._flags = None
+        dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
+        with torch.cuda.device(self.device):
+            R._ipc_free(self._base)
+        self._base = None
+
+
 def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: int = -1, rot_cos=None,
-                       rot_sin=None, group=None, compute: Optional[Callable] = None, chunks: Optional[int] = 1):
+                       rot_sin=None, group=None, compute: Optional[Callable] = None, chunks: Optional[int] = 1,
+                       out: Optional[SymmetricOutput] = None):
     """Forward attention over all ranks of `group`: every rank passes the same full
     [B, H, S, D] / [B, Hkv, KS, D] inputs, computes only its (batch, KV-head) units
     and receives the full output.  `compute` replaces the local kernel call
@@ -167,10 +284,33 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     one piece a batch split takes consecutive ranges and a single in-place
     all-gather.  chunks=None picks the count from O's size (auto_chunks).  Uneven plans gather pieces into a staging buffer and copy them
     into place; every rank takes the same collective steps (pieces that are empty
-    on some ranks are padded)."""
+    on some ranks are padded).
+
+    With `out` (a SymmetricOutput of O's shape on `group`) the gather is fused
+    into the kernels: one launch computes the rank's units and stores every O
+    tile into all ranks' buffers over NVLink, then the barrier kernel orders
+    those stores before what follows on the stream; `chunks` does not apply.
+    Returns the slot of `out` the call wrote."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     B, H, S, D = query.shape
+    if out is not None:
+        if tuple(out.shape) != (B, H, S, D):
+            raise ValueError(f"out has shape {out.shape}, the output is {(B, H, S, D)}")
+        if out.world != world or out.rank != rank:
+            raise ValueError("out was built on another process group")
+        Hkv = key.shape[1]
+        G = H // Hkv
+        me = plan(B, Hkv, world, rank)
+        dst, _ = out.next_slot()
+        if me.units():
+            qs, ks, vs = local_views(query, key, value, me)
+            mine = dst[me.b0:me.b1:me.bstep, me.g0 * G:me.g1 * G]
+            (compute or _default_compute)(qs, ks, vs, out=mine, peer_outputs=out.peer_addresses(mine),
+                                          is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
+                                          rot_sin=rot_sin)
+        out.order_stores()
+        return dst
     if chunks is None:
         chunks = auto_chunks(B, H, S, D, world, query.element_size())
     if chunks < 1:

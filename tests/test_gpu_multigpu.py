@@ -1,9 +1,12 @@
-"""flash_attn_sharded on two B200s over NCCL: every rank computes its (batch,
-KV-head group) units through the C ABI and receives the full O, which must match
-the one-GPU kernel on the same inputs (max-abs <= 2e-3, the north-star FP16 gate)
-for each gather layout: consecutive batch ranges (one piece), round-robin
-batches (several pieces, per-batch and staged collectives), a KV-head split and
-the decode KV cache viewed through strides.  Skipped with fewer than two GPUs."""
+"""flash_attn_sharded on two B200s: every rank computes its (batch, KV-head
+group) units through the C ABI and receives the full O, which must match the
+one-GPU kernel on the same inputs (max-abs <= 2e-3, the north-star FP16 gate)
+for each gather layout — consecutive batch ranges (one piece), round-robin
+batches (several pieces, per-batch and staged collectives), a KV-head split, an
+uneven split and the decode KV cache viewed through strides — both with the
+NCCL all-gather and with the gather fused into the kernels (SymmetricOutput:
+NVLink peer stores from the epilogue of the prefill, two-pass INT8 and decode
+kernels).  Skipped with fewer than two GPUs."""
 import os
 import socket
 from datetime import timedelta
@@ -60,7 +63,7 @@ def _worker(rank, port, queue):
                             device_id=torch.device("cuda", rank))
     try:
         import rdnattention_b200 as R
-        from rdnattention_b200.multigpu import flash_attn_sharded
+        from rdnattention_b200.multigpu import SymmetricOutput, flash_attn_sharded
 
         errs = {}
         for case in CASES:
@@ -69,6 +72,37 @@ def _worker(rank, port, queue):
             ref = R.flash_attn_strided(q, k, v, **kw)
             torch.cuda.synchronize()
             errs[case[0]] = (got.float() - ref.float()).abs().max().item()
+            # the fused gather, twice on different inputs: the first result stays in its slot
+            sym = SymmetricOutput(q.shape)
+            got1 = flash_attn_sharded(q, k, v, out=sym, **kw)
+            q2 = torch.flip(q, dims=(2,)).contiguous()
+            got2 = flash_attn_sharded(q2, k, v, out=sym, **kw)
+            ref2 = R.flash_attn_strided(q2, k, v, **kw)
+            torch.cuda.synchronize()
+            errs["fused_" + case[0]] = max((got1.float() - ref.float()).abs().max().item(),
+                                           (got2.float() - ref2.float()).abs().max().item())
+            sym.close()
+        # INT8 (two-pass kernel at head_dim 128, one-pass at 64): each rank computes half
+        # the batch and stores it into both ranks' outputs
+        for D in (64, 128):
+            g = torch.Generator().manual_seed(D)
+            B, H, S = 4, 8, 384
+            qi = torch.randint(-127, 128, (B, H, S, D), generator=g, dtype=torch.int8).to(rank)
+            ki = torch.randint(-127, 128, (B, H, S, D), generator=g, dtype=torch.int8).to(rank)
+            vi = torch.randint(-127, 128, (B, H, S, D), generator=g, dtype=torch.int8).to(rank)
+            qsc = (torch.rand(B, H, S, generator=g) * 0.02 + 0.001).to(rank)
+            ksc = (torch.rand(B, H, S, generator=g) * 0.02 + 0.001).to(rank)
+            ref = R.flash_attn_int8qk(qi, ki, vi, qsc, ksc, 0.01, is_causal=True)
+            sym = SymmetricOutput(qi.shape)
+            dst, _ = sym.next_slot()
+            b0, b1 = rank * B // WORLD, (rank + 1) * B // WORLD
+            mine = dst[b0:b1]
+            R.flash_attn_int8qk(qi[b0:b1], ki[b0:b1], vi[b0:b1], qsc[b0:b1], ksc[b0:b1], 0.01, is_causal=True,
+                                out=mine, peer_outputs=sym.peer_addresses(mine))
+            sym.order_stores()
+            torch.cuda.synchronize()
+            errs[f"fused_int8_d{D}"] = (dst.float() - ref.float()).abs().max().item()
+            sym.close()
         errs["status"] = R.debug_read_status()
         queue.put((rank, errs))
     finally:

@@ -29,7 +29,6 @@ _SITES = {
     0x202: "MMA issuer: K tile",
     0x204: "MMA issuer: P",
     0x203: "MMA issuer: V tile",
-    0x207: "MMA issuer: accumulator fold",
     0x101: "producer: K slot",
     0x102: "producer: V slot",
     0x301: "softmax: S",
@@ -37,8 +36,6 @@ _SITES = {
     0x304: "softmax: key scales",
     0x306: "softmax: exponent token",
     0x307: "softmax: P V",
-    0x401: "correction: P V",
-    0x402: "correction: fold request",
 }
 
 
@@ -95,3 +92,32 @@ def test_int8_expired_wait_unwinds_and_next_call_is_correct(D):
     assert R.debug_read_status() == (0, 0)
     ref = c_oracle.attention_int8(qi, ki, vi, qvec, kvec, vs, scale=np.float32(1.0) / np.sqrt(np.float32(D)))
     assert rel_rms(got, ref) < 5e-2
+
+
+def test_peer_barrier_signals_and_its_wait_expires():
+    """The cross-GPU barrier kernel of the fused all-gather, on one GPU (its
+    'peer' flag array is a local buffer).  With the other rank's word already at
+    the epoch it passes and writes the epoch into its slot of the peer's array;
+    with a word that nothing sets, its wait runs out after the debug limit,
+    records 0x401 and returns."""
+    dev = torch.device("cuda", 0)
+    peer = torch.zeros(2, dtype=torch.int32, device=dev)
+    mine = torch.tensor([0, 5], dtype=torch.int32, device=dev)
+    R._peer_barrier(2, 0, [peer.data_ptr()], mine.data_ptr(), 5, dev)
+    torch.cuda.synchronize()
+    assert peer.tolist() == [5, 0]
+    assert R.debug_read_status() == (0, 0)
+    lib = R._lib_handle()
+    lib.rdna_debug_set_wait_test(0, 1_000_000)  # barrier waits limited to 1 ms
+    try:
+        R._peer_barrier(2, 0, [peer.data_ptr()], mine.data_ptr(), 6, dev)  # word 1 stays at 5
+        torch.cuda.synchronize()
+    finally:
+        lib.rdna_debug_set_wait_test(-1, 0)
+    assert R.debug_read_status() == (0x401, 1)
+    assert peer.tolist() == [6, 0]
+    # epochs compare modulo 2^32: a word one past the wrap has reached 0xFFFFFFFF
+    mine[1] = 0
+    R._peer_barrier(2, 0, [peer.data_ptr()], mine.data_ptr(), 0xFFFFFFFF, dev)
+    torch.cuda.synchronize()
+    assert R.debug_read_status() == (0, 0)
