@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from rdnattention_b200.multigpu import _uniform_axis, flash_attn_sharded, local_views, pieces, plan
+from rdnattention_b200.multigpu import SymmetricOutput, _uniform_axis, flash_attn_sharded, local_views, pieces, plan
 
 
 @pytest.mark.parametrize("B,Hkv,world", [(4, 8, 2), (1, 8, 2), (3, 2, 2), (1, 1, 2), (8, 8, 8), (2, 3, 4), (5, 8, 8),
@@ -154,3 +154,29 @@ def test_sharded_forward_in_place_on_four_ranks(shape, world, chunks):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert results == {r: True for r in range(world)}
+
+
+def test_symmetric_output_slots_and_peer_addresses():
+    """The fused gather's host bookkeeping (no GPU: the object is assembled over a
+    host buffer): slots are used in turn, and a view of this rank's slot maps to the
+    same offset in every peer's allocation."""
+    shape = (2, 4, 8, 16)
+    n = 2 * 4 * 8 * 16
+    buf = torch.empty(2 * n, dtype=torch.float16)
+    so = SymmetricOutput.__new__(SymmetricOutput)
+    so._base = buf.data_ptr()
+    so.slot_bytes = n * 2
+    so.slots = [buf[:n].view(shape), buf[n:].view(shape)]
+    so._turn = 0
+    so._peer_bases = [1 << 40, 3 << 40]
+    first, off0 = so.next_slot()
+    second, off1 = so.next_slot()
+    third, _ = so.next_slot()
+    assert first.data_ptr() == buf.data_ptr() and off0 == 0
+    assert second.data_ptr() == buf.data_ptr() + n * 2 and off1 == n * 2
+    assert third.data_ptr() == first.data_ptr()
+    view = second[1::2, 2:4]  # a rank's round-robin units of two KV heads
+    off = view.data_ptr() - buf.data_ptr()
+    assert so.peer_addresses(view) == [(1 << 40) + off, (3 << 40) + off]
+    with pytest.raises(ValueError):
+        so.peer_addresses(torch.empty(4, dtype=torch.float16))
