@@ -63,10 +63,10 @@ def _prefill_traits(name):
 
 
 def _launch_regs(t):
-    """Traits::LAUNCH_REGS / RESPLIT (fa_prefill.cuh): FP16 one-tile double-buffered kernels
-    run two CTAs per SM at 128 registers; two-tile kernels launch at the most their thread
-    count allows (384 threads: 168); both re-split them."""
-    min_blocks = 2 if (t["NT"] == 1 and t["SDB"] and not t["I8"]) else 1
+    """Traits::LAUNCH_REGS / RESPLIT (fa_prefill.cuh): one-tile double-buffered kernels (FP16,
+    and INT8 at head_dim 64) run two CTAs per SM at 128 registers; two-tile kernels launch at
+    the most their thread count allows (384 threads: 168); both re-split them."""
+    min_blocks = 2 if (t["NT"] == 1 and t["SDB"]) else 1
     resplit = t["NT"] == 2 or min_blocks == 2
     threads = 128 * t["NT"] + 128
     return (128 if min_blocks == 2 else (65536 // threads) // 8 * 8) if resplit else None
