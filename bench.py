@@ -740,6 +740,17 @@ def main():
         u = torch.tensor([units_rank], device="cuda", dtype=torch.int64)
         torch.distributed.all_reduce(u, op=torch.distributed.ReduceOp.MAX)
         compute["units_per_rank_max"] = int(u.item())
+    # The roofline's kernel time: the attention kernel alone, from CUDA events the
+    # library records right around its launch (not around the RoPE pre-pass), in a
+    # separate pass of the same steps after the timed region (the event between the
+    # pre-pass and the kernel would cost their overlap inside it).  N > 1: the
+    # rank's own units (the compute-only step), max over ranks.
+    k_turn = turn if not dist_on else cturn
+    kernel_ms = R.debug_time_kernel(lambda: next(k_turn)(), repeats=max(5, min(args.steps, 20)))
+    if dist_on:
+        km = torch.tensor([kernel_ms], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(km, op=torch.distributed.ReduceOp.MAX)
+        kernel_ms = km.item()
     status = R.debug_read_status()
     value = per_step_units * args.steps / (ms / 1e3) / scale
     ms_step = ms / args.steps
@@ -765,8 +776,8 @@ def main():
 
     metric, unit = metric_of(cfg)
     peak_tc, peak_hbm, peak_src = load_peaks()
-    # the roofline is the per-GPU kernel's: at N > 1 the compute-only time of the rank's units
-    k_ms = compute["ms_per_step"] if compute else ms_step
+    # the roofline is the per-GPU attention kernel's (at N > 1 on the rank's own units)
+    k_ms = kernel_ms
     k_units = per_step_units * (compute["units_per_rank_max"] / (cfg["B"] * cfg["Hkv"]) if compute else 1.0)
     if cfg["kind"] == "decode":
         roof = {"bound": "hbm", "achieved": k_units / (k_ms / 1e3) / 1e9, "peak": peak_hbm, "unit": "GB/s"}
@@ -781,6 +792,9 @@ def main():
                 "unit": "TOP/s" if cfg["kind"] == "int8" else "TFLOP/s"}
         peak_src = src
     roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["kernel_ms"] = kernel_ms
+    roof["timing"] = ("attention kernel alone: CUDA events recorded by the library right around its launch "
+                      "(rdna_debug_set_kernel_events), a pass of the same steps after the timed region")
     roof["peak_source"] = peak_src if cfg["kind"] != "decode" else f"{peak_src} (MEASURED_PEAKS.json copy)"
     spec = SPEC_PEAKS["hbm" if cfg["kind"] == "decode" else cfg["kind"] if cfg["kind"] == "int8" else "fp16"]
     roof["spec_peak"] = spec

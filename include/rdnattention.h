@@ -218,6 +218,14 @@ RDNA_API int32_t rdna_debug_read_status(int32_t* out2);
  * and the next call without the hook is unaffected.  Always returns 0. */
 RDNA_API int32_t rdna_debug_set_wait_test(int32_t withhold_block, uint64_t wait_limit_ns);
 
+/* Debug (extension): a timing hook.  Until it is called again with NULLs,
+ * forward calls made by the calling thread record start_event (a cudaEvent_t)
+ * on their stream right before launching their attention kernel (prefill or
+ * decode) and stop_event right after it, so the caller can time that kernel
+ * alone, without the RoPE pre-pass; the event between the two serialises them
+ * (no programmatic overlap of the pre-pass tail).  Always returns 0. */
+RDNA_API int32_t rdna_debug_set_kernel_events(void* start_event, void* stop_event);
+
 /* ---- Multi-GPU (extension, no counterpart in the single-device reference) ----
  *
  * The all-gather of the output across the GPUs of one node, fused into the

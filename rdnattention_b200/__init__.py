@@ -107,6 +107,8 @@ def _lib_handle():
         lib.rdna_ipc_free.restype = i32
         lib.rdna_peer_barrier.argtypes = [i32, i32, pp, vp, u32, vp]
         lib.rdna_peer_barrier.restype = i32
+        lib.rdna_debug_set_kernel_events.argtypes = [vp, vp]
+        lib.rdna_debug_set_kernel_events.restype = i32
         _lib = lib
     return _lib
 
@@ -539,6 +541,30 @@ def flash_attn_int8qk_quantized(query, key, value, is_causal: bool = False, wind
     if rc != 0:
         raise RDNAttentionError(f"flash_attn_int8qk failed: {_last_error()}")
     return out
+
+
+def debug_time_kernel(call, repeats: int = 10) -> float:
+    """Average device time (ms) of the attention kernel that `call()` launches
+    (through any of this library's forward entry points, on the current thread),
+    timed by CUDA events the library records right around that kernel's launch
+    (rdna_debug_set_kernel_events), so a RoPE pre-pass in the same call is not
+    counted.  Debug extension; synchronises the device."""
+    import torch
+
+    lib = _lib_handle()
+    total = 0.0
+    for _ in range(repeats):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()  # creates the CUDA events; the library re-records them
+        stop.record()
+        lib.rdna_debug_set_kernel_events(start.cuda_event, stop.cuda_event)
+        try:
+            call()
+        finally:
+            lib.rdna_debug_set_kernel_events(None, None)
+        stop.synchronize()
+        total += start.elapsed_time(stop)
+    return total / repeats
 
 
 def debug_read_status():

@@ -14,6 +14,7 @@
 namespace rdna {
 int debugReadStatus(int32_t* out2, const char** why);
 void debugSetWaitTest(int32_t withhold_block, uint64_t wait_limit_ns);
+void debugSetKernelEvents(void* start, void* stop);
 }
 
 namespace {
@@ -467,5 +468,10 @@ RDNA_API int32_t rdna_debug_read_status(int32_t* out2) {
 
 RDNA_API int32_t rdna_debug_set_wait_test(int32_t withhold_block, uint64_t wait_limit_ns) {
     rdna::debugSetWaitTest(withhold_block, wait_limit_ns);
+    return 0;
+}
+
+RDNA_API int32_t rdna_debug_set_kernel_events(void* start_event, void* stop_event) {
+    rdna::debugSetKernelEvents(start_event, stop_event);
     return 0;
 }

@@ -111,6 +111,19 @@ uint64_t bc_extent(uint64_t n, bool bcast) { return bcast ? 1u : n; }
 thread_local int g_dbg_withhold = -1;
 thread_local unsigned long long g_dbg_wait_limit_ns = 0;
 
+// Debug timing hook of the calling thread (rdna_debug_set_kernel_events): events
+// recorded right before and right after the launch of each call's attention
+// kernel (prefill or decode), not around the RoPE pre-pass.
+thread_local cudaEvent_t g_dbg_ev[2] = {nullptr, nullptr};
+
+template <class F>
+cudaError_t launch_timed(cudaStream_t st, const F& launch) {
+    if (g_dbg_ev[0] != nullptr) cudaEventRecord(g_dbg_ev[0], st);
+    cudaError_t e = launch();
+    if (g_dbg_ev[1] != nullptr) cudaEventRecord(g_dbg_ev[1], st);
+    return e;
+}
+
 // Output replicas of the call in progress on this thread (the *Peers entry
 // points set them for the duration of one call): other GPUs' counterparts of
 // the output pointer, which every kernel writes with the same values as O.
@@ -274,7 +287,7 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    ce = cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, tmO, p);
+    ce = launch_timed(stream, [&] { return cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, tmO, p); });
     if (ce == cudaSuccess) ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
     return 0;
@@ -510,13 +523,13 @@ int launch_f16(char* err, const ForwardParams& a, cudaStream_t stream) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         return e == cudaSuccess ? cudaLaunchKernelEx(&cfg, kern, tmK, tmV, p) : e;
     };
-    cudaError_t ce;
-    if (D == 64)
-        ce = p.rope ? launch(fa_decode_kernel<64, true>, Layout<64>::SMEM_BYTES)
-                    : launch(fa_decode_kernel<64, false>, Layout<64>::SMEM_BYTES);
-    else
-        ce = p.rope ? launch(fa_decode_kernel<128, true>, Layout<128>::SMEM_BYTES)
-                    : launch(fa_decode_kernel<128, false>, Layout<128>::SMEM_BYTES);
+    cudaError_t ce = launch_timed(stream, [&] {
+        if (D == 64)
+            return p.rope ? launch(fa_decode_kernel<64, true>, Layout<64>::SMEM_BYTES)
+                          : launch(fa_decode_kernel<64, false>, Layout<64>::SMEM_BYTES);
+        return p.rope ? launch(fa_decode_kernel<128, true>, Layout<128>::SMEM_BYTES)
+                      : launch(fa_decode_kernel<128, false>, Layout<128>::SMEM_BYTES);
+    });
     if (ce == cudaSuccess) ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
     return 0;
@@ -804,6 +817,11 @@ int quantizeInt8QKV(const QuantizeInt8Params& a, void* stream) {
     const cudaError_t ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(g_err_i8, "%s", cudaGetErrorString(ce));
     return 0;
+}
+
+void debugSetKernelEvents(void* start, void* stop) {
+    g_dbg_ev[0] = static_cast<cudaEvent_t>(start);
+    g_dbg_ev[1] = static_cast<cudaEvent_t>(stop);
 }
 
 void debugSetWaitTest(int32_t withhold_block, uint64_t wait_limit_ns) {

@@ -310,3 +310,30 @@ def test_kv_stride_zero_broadcast(S, KS, causal, rope, axis):
     ref = c_oracle.attention_f16(q, k.contiguous(), v.contiguous(), causal=causal, rot_cos=cos, rot_sin=sin)
     err = (got.double() - ref).abs()
     assert err.max().item() <= 2e-3 and err.mean().item() <= 2e-4
+
+
+def test_kernel_timing_hook_times_the_attention_kernel_alone():
+    """rdna_debug_set_kernel_events: the events bracket the attention kernel of a
+    RoPE call (not its K pre-pass), the output is unchanged, and the hook is off
+    again afterwards."""
+    B, H, Hkv, S, D = 2, 8, 2, 2048, 128
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(B, H, S, D, generator=g).half().cuda()
+    k = torch.randn(B, Hkv, S, D, generator=g).half().cuda()
+    v = torch.randn(B, Hkv, S, D, generator=g).half().cuda()
+    cos, sin = rope_tables(S, D, 500000.0, device="cuda")
+    ref = R.flash_attn(q, k, v, is_causal=True, rot_cos=cos, rot_sin=sin)
+    outs = []
+    kernel_ms = R.debug_time_kernel(
+        lambda: outs.append(R.flash_attn(q, k, v, is_causal=True, rot_cos=cos, rot_sin=sin)), repeats=5)
+    torch.cuda.synchronize()
+    assert all(torch.equal(o, ref) for o in outs) and len(outs) == 5
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(5):
+        R.flash_attn(q, k, v, is_causal=True, rot_cos=cos, rot_sin=sin)
+    e.record()
+    torch.cuda.synchronize()
+    call_ms = s.elapsed_time(e) / 5
+    assert 0.0 < kernel_ms < call_ms * 1.05, (kernel_ms, call_ms)
+    assert R.debug_read_status() == (0, 0)
