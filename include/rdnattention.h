@@ -129,9 +129,10 @@ RDNA_API int32_t rdna_attention_forward_ws(
  * total over the batch fit, 20480 do not) returns -3 with a message naming
  * the limit.  Without RoPE no workspace is used.  The first call on a
  * device looks up the array's device address on that device; make that
- * first call before any stream capture.  All calls share the one array:
- * calls that overlap on the GPU (different streams or threads) race on it,
- * so serialise them. */
+ * first call before any stream capture; the address is kept for the life
+ * of the process, so calls after cudaDeviceReset are unsupported.  All
+ * calls share the one array: calls that overlap on the GPU (different
+ * streams or threads) race on it, so serialise them. */
 RDNA_API int32_t rdna_attention_forward_noalloc(
     const void* q, const void* k, const void* v, void* output,
     const void* rot_cos, const void* rot_sin,
