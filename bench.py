@@ -206,8 +206,25 @@ def sharded_step_fns(cfg, x, world, rank, chunks, sym=None):
     if cfg["kind"] == "fp16":
         kw = dict(is_causal=cfg["causal"], window_size=cfg["window"], rot_cos=x.get("cos"), rot_sin=x.get("sin"))
     shard = M.plan(cfg["B"], cfg["Hkv"], world, rank, interleave=sym is not None or chunks > 1)
-    qs, ks, vs = M.local_views(x["q"], x["k"], x["v"], shard)
+    names = ("qi", "ki", "vi") if cfg["kind"] == "int8" else ("q", "k", "v")
+    qs, ks, vs = M.local_views(*(x[n] for n in names), shard)
     out = torch.empty(qs.shape, dtype=torch.float16, device="cuda")
+
+    if cfg["kind"] == "int8":
+        G = cfg["H"] // cfg["Hkv"]
+        bsl = slice(shard.b0, shard.b1, shard.bstep)
+        qsc = x["qsc"][bsl, shard.g0 * G:shard.g1 * G].contiguous()
+        ksc = x["ksc"][bsl, shard.g0:shard.g1].contiguous()
+
+        def full():
+            return M.flash_attn_int8qk_sharded(x["qi"], x["ki"], x["vi"], x["qsc"], x["ksc"], x["vs"],
+                                               out=sym, chunks=chunks)
+
+        def compute_only():
+            if qs.numel():
+                R.flash_attn_int8qk_strided(qs, ks, vs, qsc, ksc, x["vs"], out=out)
+
+        return full, compute_only, shard
 
     def full():
         if sym is not None:
@@ -380,16 +397,21 @@ def time_e2e_sharded(cfg, x, steps, warmup, world, rank, chunks=1, sym=None):
     from rdnattention_b200 import multigpu as M
 
     shard = M.plan(cfg["B"], cfg["Hkv"], world, rank, interleave=sym is not None or chunks > 1)
-    qs, ks, vs = M.local_views(x["q"], x["k"], x["v"], shard)
+    int8 = cfg["kind"] == "int8"
+    G = cfg["H"] // cfg["Hkv"]
+    qs, ks, vs = M.local_views(*(x[n] for n in (("qi", "ki", "vi") if int8 else ("q", "k", "v"))), shard)
     host = {"q": qs.contiguous().cpu().pin_memory(), "k": ks.contiguous().cpu().pin_memory(),
             "v": vs.contiguous().cpu().pin_memory()}
+    if int8:
+        bsl = slice(shard.b0, shard.b1, shard.bstep)
+        host["qsc"] = x["qsc"][bsl, shard.g0 * G:shard.g1 * G].contiguous().cpu().pin_memory()
+        host["ksc"] = x["ksc"][bsl, shard.g0:shard.g1].contiguous().cpu().pin_memory()
     rope = "cos" in x and cfg["kind"] == "fp16"
     if rope:
         host["cos"], host["sin"] = x["cos"].cpu().pin_memory(), x["sin"].cpu().pin_memory()
     dev = {n: torch.empty_like(t, device="cuda") for n, t in host.items()}
     out_local = torch.empty(host["q"].shape, dtype=torch.float16, device="cuda")
     out_host = torch.empty(out_local.shape, dtype=torch.float16).pin_memory()
-    G = cfg["H"] // cfg["Hkv"]
     elems = shard.units() * G * cfg["S"] * cfg["D"]
     units = [M.plan(cfg["B"], cfg["Hkv"], world, r, interleave=chunks > 1) for r in range(world)]
     cap = max(u.units() for u in units) * G * cfg["S"] * cfg["D"]
@@ -399,6 +421,14 @@ def time_e2e_sharded(cfg, x, steps, warmup, world, rank, chunks=1, sym=None):
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = out_host.numel() * out_host.element_size()
 
+    def local(o, peers=None):
+        if int8:
+            R.flash_attn_int8qk_strided(dev["q"], dev["k"], dev["v"], dev["qsc"], dev["ksc"], x["vs"], out=o,
+                                        peer_outputs=peers)
+        else:
+            R.flash_attn_strided(dev["q"], dev["k"], dev["v"], out=o, rot_cos=dev.get("cos"),
+                                 rot_sin=dev.get("sin"), peer_outputs=peers, **kw)
+
     def step():
         for n in host:
             dev[n].copy_(host[n], non_blocking=True)
@@ -406,14 +436,12 @@ def time_e2e_sharded(cfg, x, steps, warmup, world, rank, chunks=1, sym=None):
             dst, _ = sym.next_slot()
             mine = dst[shard.b0:shard.b1:shard.bstep, shard.g0 * G:shard.g1 * G]
             if qs.numel():
-                R.flash_attn_strided(dev["q"], dev["k"], dev["v"], out=mine, rot_cos=dev.get("cos"),
-                                     rot_sin=dev.get("sin"), peer_outputs=sym.peer_addresses(mine), **kw)
+                local(mine, sym.peer_addresses(mine))
             sym.order_stores()
             out_host.copy_(mine, non_blocking=True)
             return
         if qs.numel():
-            R.flash_attn_strided(dev["q"], dev["k"], dev["v"], out=out_local, rot_cos=dev.get("cos"),
-                                 rot_sin=dev.get("sin"), **kw)
+            local(out_local)
         send[:elems].copy_(out_local.reshape(-1))
         torch.distributed.all_gather_into_tensor(recv, send)
         out_host.copy_(out_local, non_blocking=True)
@@ -721,8 +749,6 @@ def main():
         ms = time_device(lambda: next(turn)(), args.steps, args.warmup, dist_on, sampler)
         shard = None
     else:
-        if cfg["kind"] == "int8":
-            raise SystemExit("the sharded INT8 step is not wired into the bench (use --config 2/4a/4b/5)")
         if args.gather == "fused":
             from rdnattention_b200.multigpu import SymmetricOutput
 

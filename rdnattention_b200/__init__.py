@@ -336,9 +336,25 @@ def flash_attn_int8qk(query, key, value, q_scale, k_scale, v_scale: float, is_ca
     ``peer_outputs`` as in flash_attn_strided (other GPUs' counterparts of
     ``out`` that the kernel also writes).
     """
+    return _int8_forward(query, key, value, q_scale, k_scale, v_scale, is_causal, window_size, out, peer_outputs,
+                         True)
+
+
+def flash_attn_int8qk_strided(query, key, value, q_scale, k_scale, v_scale: float, is_causal: bool = False,
+                              window_size: int = -1, out=None, peer_outputs=None):
+    """flash_attn_int8qk over arbitrary batch/head/seq strides (head_dim
+    contiguous), e.g. the views of one rank's units in a multi-GPU split;
+    per-token scale tensors may be strided views too (they are made contiguous).
+    Extension: the reference reaches strided INT8 only through its raw C ABI."""
+    return _int8_forward(query, key, value, q_scale, k_scale, v_scale, is_causal, window_size, out, peer_outputs,
+                         False)
+
+
+def _int8_forward(query, key, value, q_scale, k_scale, v_scale, is_causal, window_size, out, peer_outputs,
+                  require_contiguous):
     import torch
 
-    _validate_inputs(query, key, value, torch.int8)
+    _validate_inputs(query, key, value, torch.int8, require_contiguous)
     batch, heads, seq_len, head_dim = query.shape
     _, kv_heads, key_seq_len, _ = key.shape
     _check_head_dim(head_dim, "flash_attn_int8qk", allowed=SUPPORTED_HEAD_DIMS_INT8)

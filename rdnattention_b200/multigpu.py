@@ -267,7 +267,7 @@ class SymmetricOutput:
 
 def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: int = -1, rot_cos=None,
                        rot_sin=None, group=None, compute: Optional[Callable] = None, chunks: Optional[int] = 1,
-                       out: Optional[SymmetricOutput] = None):
+                       out: Optional[SymmetricOutput] = None, q_side=None, kv_side=None):
     """Forward attention over all ranks of `group`: every rank passes the same full
     [B, H, S, D] / [B, Hkv, KS, D] inputs, computes only its (batch, KV-head) units
     and receives the full output.  `compute` replaces the local kernel call
@@ -290,45 +290,58 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     into the kernels: one launch computes the rank's units and stores every O
     tile into all ranks' buffers over NVLink, then the barrier kernel orders
     those stores before what follows on the stream; `chunks` does not apply.
-    Returns the slot of `out` the call wrote."""
+    Returns the slot of `out` the call wrote.
+
+    `q_side` / `kv_side`: per-row companions of the query / key tensors (e.g. the
+    INT8 per-token scales, [B, H, S] / [B, Hkv, KS]), sliced with each shard like
+    them and passed to `compute` under those names; scalars pass through.  The
+    output is float16 whatever the input type."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     B, H, S, D = query.shape
+    odt = torch.float16
+    Hkv = key.shape[1]
+    G = H // Hkv
+    compute = compute or _default_compute
+
+    def run(piece, out_view=None, peers=None):
+        """The local kernel call for one rectangle of units."""
+        qs, ks, vs = local_views(query, key, value, piece)
+        kw = dict(is_causal=is_causal, window_size=window_size, rot_cos=rot_cos, rot_sin=rot_sin)
+        bsl = slice(piece.b0, piece.b1, piece.bstep)
+        if q_side is not None:
+            kw["q_side"] = q_side[bsl, piece.g0 * G:piece.g1 * G] if torch.is_tensor(q_side) else q_side
+        if kv_side is not None:
+            kw["kv_side"] = kv_side[bsl, piece.g0:piece.g1] if torch.is_tensor(kv_side) else kv_side
+        if peers is not None:
+            kw["peer_outputs"] = peers
+        return compute(qs, ks, vs, out=out_view, **kw)
+
     if out is not None:
         if tuple(out.shape) != (B, H, S, D):
             raise ValueError(f"out has shape {out.shape}, the output is {(B, H, S, D)}")
         if out.world != world or out.rank != rank:
             raise ValueError("out was built on another process group")
-        Hkv = key.shape[1]
-        G = H // Hkv
         me = plan(B, Hkv, world, rank)
         dst, _ = out.next_slot()
         if me.units():
-            qs, ks, vs = local_views(query, key, value, me)
             mine = dst[me.b0:me.b1:me.bstep, me.g0 * G:me.g1 * G]
-            (compute or _default_compute)(qs, ks, vs, out=mine, peer_outputs=out.peer_addresses(mine),
-                                          is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
-                                          rot_sin=rot_sin)
+            run(me, mine, out.peer_addresses(mine))
         out.order_stores()
         return dst
     if chunks is None:
-        chunks = auto_chunks(B, H, S, D, world, query.element_size())
+        chunks = auto_chunks(B, H, S, D, world, 2)
     if chunks < 1:
         raise ValueError("chunks must be >= 1")
-    Hkv = key.shape[1]
-    G = H // Hkv
-    compute = compute or _default_compute
     shards = [plan(B, Hkv, world, r, interleave=chunks > 1) for r in range(world)]
     axis = _uniform_axis(shards, Hkv)
     if axis == "batch_block":
         # One piece, consecutive batch ranges: the rank fills its contiguous block of O
         # and one in-place all-gather assembles the rest around it.
-        out = torch.empty(B, H, S, D, dtype=query.dtype, device=query.device)
+        out = torch.empty(B, H, S, D, dtype=odt, device=query.device)
         me = shards[rank]
-        qs, ks, vs = local_views(query, key, value, me)
         mine = out[me.b0:me.b1]
-        compute(qs, ks, vs, out=mine, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
-                rot_sin=rot_sin)
+        run(me, mine)
         dist.all_gather_into_tensor(out.view(-1), mine.view(-1), group=group)
         return out
     if axis is not None:
@@ -339,7 +352,7 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
         # staging buffer and no reassembly copy.  The rank's units run in `chunks`
         # pieces of batch elements; each piece's collectives (asynchronous, on NCCL's
         # stream) overlap the next piece's kernel.
-        out = torch.empty(B, H, S, D, dtype=query.dtype, device=query.device)
+        out = torch.empty(B, H, S, D, dtype=odt, device=query.device)
         me = shards[rank]
         h0, h1 = me.g0 * G, me.g1 * G
         nb = len(me.batches) if axis == "batch" else B
@@ -350,10 +363,8 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
                 piece = Shard("batch", me.b0 + lo * world, me.b0 + hi * world, me.g0, me.g1, world)
             else:
                 piece = Shard("kv_head", lo, hi, me.g0, me.g1)
-            qs, ks, vs = local_views(query, key, value, piece)
             mine = out[piece.b0:piece.b1:piece.bstep, h0:h1]
-            compute(qs, ks, vs, out=mine, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
-                    rot_sin=rot_sin)
+            run(piece, mine)
             if axis == "batch" and len(piece.batches) > 1:
                 # several batch elements of every rank, interleaved in O: one staged
                 # collective (cheap when O per batch element is small, e.g. decode)
@@ -389,22 +400,20 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
         cap = max(sizes)  # every rank contributes the same number of elements
         if cap == 0:
             continue
-        send = torch.zeros(cap, dtype=query.dtype, device=query.device) if sizes[rank] < cap else None
+        send = torch.zeros(cap, dtype=odt, device=query.device) if sizes[rank] < cap else None
         if sizes[rank] > 0:
-            qs, ks, vs = local_views(query, key, value, per_rank[rank][c])
-            o_local = compute(qs, ks, vs, is_causal=is_causal, window_size=window_size, rot_cos=rot_cos,
-                              rot_sin=rot_sin).reshape(-1)
+            o_local = run(per_rank[rank][c]).reshape(-1)
             if send is None:
                 send = o_local
             else:
                 send[:sizes[rank]] = o_local
-        recv = torch.empty(world * cap, dtype=query.dtype, device=query.device)
+        recv = torch.empty(world * cap, dtype=odt, device=query.device)
         works.append(dist.all_gather_into_tensor(recv, send, group=group, async_op=True))
         gathered.append((c, cap, sizes, recv))
     for w in works:
         w.wait()
 
-    out = torch.empty(B, H, S, D, dtype=query.dtype, device=query.device)
+    out = torch.empty(B, H, S, D, dtype=odt, device=query.device)
     for c, cap, sizes, recv in gathered:
         for r in range(world):
             if sizes[r] == 0:
@@ -413,3 +422,27 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
             block = recv[r * cap:r * cap + sizes[r]].view(len(s.batches), (s.g1 - s.g0) * G, S, D)
             out[s.b0:s.b1:s.bstep, s.g0 * G:s.g1 * G] = block
     return out
+
+
+def _int8_compute(v_scale):
+    from . import flash_attn_int8qk_strided
+
+    def compute(q, k, v, out=None, peer_outputs=None, q_side=None, kv_side=None, is_causal=False, window_size=-1,
+                rot_cos=None, rot_sin=None):
+        return flash_attn_int8qk_strided(q, k, v, q_side, kv_side, v_scale, is_causal, window_size, out=out,
+                                         peer_outputs=peer_outputs)
+
+    return compute
+
+
+def flash_attn_int8qk_sharded(query, key, value, q_scale, k_scale, v_scale: float, is_causal: bool = False,
+                              window_size: int = -1, group=None, chunks: Optional[int] = 1,
+                              out: Optional[SymmetricOutput] = None):
+    """flash_attn_int8qk over all ranks of `group` (same arguments, plus the
+    gather options of flash_attn_sharded): every rank passes the same full int8
+    inputs and per-token scales, computes its (batch, KV-head) units — the
+    scales sliced with them — and receives the full float16 output, fused into
+    the kernels with `out=SymmetricOutput(...)` or through NCCL otherwise."""
+    return flash_attn_sharded(query, key, value, is_causal=is_causal, window_size=window_size, group=group,
+                              compute=_int8_compute(v_scale), chunks=chunks, out=out, q_side=q_scale,
+                              kv_side=k_scale)

@@ -63,7 +63,7 @@ def _worker(rank, port, queue):
                             device_id=torch.device("cuda", rank))
     try:
         import rdnattention_b200 as R
-        from rdnattention_b200.multigpu import SymmetricOutput, flash_attn_sharded
+        from rdnattention_b200.multigpu import SymmetricOutput, flash_attn_int8qk_sharded, flash_attn_sharded
 
         errs = {}
         for case in CASES:
@@ -82,26 +82,23 @@ def _worker(rank, port, queue):
             errs["fused_" + case[0]] = max((got1.float() - ref.float()).abs().max().item(),
                                            (got2.float() - ref2.float()).abs().max().item())
             sym.close()
-        # INT8 (two-pass kernel at head_dim 128, one-pass at 64): each rank computes half
-        # the batch and stores it into both ranks' outputs
+        # INT8 (two-pass kernel at head_dim 128, one-pass at 64), per-token Q/K scales sliced
+        # with each rank's units: the NCCL gather and the fused one
         for D in (64, 128):
             g = torch.Generator().manual_seed(D)
-            B, H, S = WORLD * 2, 8, 384
+            B, H, Hkv, S = WORLD * 2, 8, 4, 384
             qi = torch.randint(-127, 128, (B, H, S, D), generator=g, dtype=torch.int8).to(rank)
-            ki = torch.randint(-127, 128, (B, H, S, D), generator=g, dtype=torch.int8).to(rank)
-            vi = torch.randint(-127, 128, (B, H, S, D), generator=g, dtype=torch.int8).to(rank)
+            ki = torch.randint(-127, 128, (B, Hkv, S, D), generator=g, dtype=torch.int8).to(rank)
+            vi = torch.randint(-127, 128, (B, Hkv, S, D), generator=g, dtype=torch.int8).to(rank)
             qsc = (torch.rand(B, H, S, generator=g) * 0.02 + 0.001).to(rank)
-            ksc = (torch.rand(B, H, S, generator=g) * 0.02 + 0.001).to(rank)
+            ksc = (torch.rand(B, Hkv, S, generator=g) * 0.02 + 0.001).to(rank)
             ref = R.flash_attn_int8qk(qi, ki, vi, qsc, ksc, 0.01, is_causal=True)
+            got = flash_attn_int8qk_sharded(qi, ki, vi, qsc, ksc, 0.01, is_causal=True)
             sym = SymmetricOutput(qi.shape)
-            dst, _ = sym.next_slot()
-            b0, b1 = rank * B // WORLD, (rank + 1) * B // WORLD
-            mine = dst[b0:b1]
-            R.flash_attn_int8qk(qi[b0:b1], ki[b0:b1], vi[b0:b1], qsc[b0:b1], ksc[b0:b1], 0.01, is_causal=True,
-                                out=mine, peer_outputs=sym.peer_addresses(mine))
-            sym.order_stores()
+            fused = flash_attn_int8qk_sharded(qi, ki, vi, qsc, ksc, 0.01, is_causal=True, out=sym)
             torch.cuda.synchronize()
-            errs[f"fused_int8_d{D}"] = (dst.float() - ref.float()).abs().max().item()
+            errs[f"int8_d{D}"] = (got.float() - ref.float()).abs().max().item()
+            errs[f"fused_int8_d{D}"] = (fused.float() - ref.float()).abs().max().item()
             sym.close()
         errs["status"] = R.debug_read_status()
         queue.put((rank, errs))

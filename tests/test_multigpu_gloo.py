@@ -180,3 +180,57 @@ def test_symmetric_output_slots_and_peer_addresses():
     assert so.peer_addresses(view) == [(1 << 40) + off, (3 << 40) + off]
     with pytest.raises(ValueError):
         so.peer_addresses(torch.empty(4, dtype=torch.float16))
+
+
+def _int8_worker(rank, world, port, shape, chunks, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import c_oracle
+
+        B, H, Hkv, S, D = shape
+        g = torch.Generator().manual_seed(5)  # every rank holds the same full inputs
+        qi = torch.randint(-127, 128, (B, H, S, D), generator=g, dtype=torch.int8)
+        ki = torch.randint(-127, 128, (B, Hkv, S, D), generator=g, dtype=torch.int8)
+        vi = torch.randint(-127, 128, (B, Hkv, S, D), generator=g, dtype=torch.int8)
+        qsc = torch.rand(B, H, S, generator=g) * 0.02 + 0.001
+        ksc = torch.rand(B, Hkv, S, generator=g) * 0.02 + 0.001
+
+        def compute(q, k, v, out=None, q_side=None, kv_side=None, **kw):
+            # the shard's own per-token scales arrive sliced like its Q and K
+            assert q_side.shape == q.shape[:3] and kv_side.shape == k.shape[:3]
+            o = c_oracle.attention_int8(q, k, v, q_side.contiguous(), kv_side.contiguous(), 0.01,
+                                        causal=kw["is_causal"]).half()
+            if out is not None:
+                out.copy_(o)
+            return o
+
+        got = flash_attn_sharded(qi, ki, vi, is_causal=True, compute=compute, chunks=chunks, q_side=qsc,
+                                 kv_side=ksc)
+        ref = c_oracle.attention_int8(qi, ki, vi, qsc, ksc, 0.01, causal=True).half()
+        queue.put((rank, got.dtype == torch.float16 and torch.equal(got, ref)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("shape,world,chunks", [
+    ((4, 4, 2, 24, 32), 2, 1),   # consecutive batch ranges
+    ((4, 4, 2, 24, 32), 2, 2),   # round robin in two pieces
+    ((1, 8, 4, 17, 32), 2, 1),   # KV-head split: the scales' head axis is sliced too
+    ((3, 4, 2, 9, 32), 2, 1),    # uneven: staged gather
+])
+def test_int8_sharded_slices_the_per_token_scales(shape, world, chunks):
+    """INT8 sharding: each rank's compute receives its units' per-token Q/K
+    scales (q_side / kv_side sliced like Q and K) and the gathered float16
+    output equals the single-device oracle."""
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_int8_worker, args=(r, world, port, shape, chunks, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert results == {r: True for r in range(world)}
