@@ -115,7 +115,7 @@ bool hasDevice();
 /// Multi-GPU extensions.  forwardF16Ws / forwardInt8QK that also write the output
 /// to `n_peers` (<= 7) other GPUs' counterparts of params.o: same strides,
 /// mapped into this process (ipcOpen), 16-byte aligned.  The all-gather of the
-/// output is fused into the kernels' epilogues as NVLink peer stores; the peers
+/// output is fused into the kernels' epilogues as TMA stores to the peers; the peers
 /// may read them once this call's kernels have completed.
 int forwardF16WsPeers(const ForwardParams& params, void* workspace, size_t workspace_bytes, int n_peers,
                       void* const* peers, void* stream);

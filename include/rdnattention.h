@@ -233,8 +233,9 @@ RDNA_API int32_t rdna_debug_set_kernel_events(void* start_event, void* stop_even
  * kernels: a *_peers call also writes every output element to each of the
  * n_peers (0..7) buffers in peer_outputs, the other GPUs' counterparts of
  * `output` (same strides, mapped into this process with rdna_ipc_open,
- * 16-byte aligned), with 16-byte stores over NVLink from the epilogue of each
- * output tile, so the transfer overlaps the tiles still being computed.  The
+ * 16-byte aligned): the epilogue of each output tile stores it by TMA into
+ * every peer's buffer over NVLink (the decode kernel with 16-byte stores), so
+ * the transfer overlaps the tiles still being computed.  The
  * peers may read the values once this call's kernels have completed (order
  * their reads after it, e.g. with a collective on the same stream). */
 

@@ -42,9 +42,9 @@
 // warps (T::ROPE_Q kernels) or by the same pre-pass.
 //
 // Output replicas (Params::n_peer > 0, the multi-GPU all-gather fused into the
-// kernel): after the TMA store of a tile's O, the tile's softmax warps copy the
-// staged tile to the same place in each peer GPU's output with 16-byte stores
-// over NVLink, so the gather overlaps the CTAs still computing.
+// kernel): the staged tile of O is stored by TMA into the local output and into
+// each peer GPU's output (one tensor map per peer, the same box coordinates),
+// so the gather crosses NVLink while the CTAs after it compute.
 //
 // TMEM columns: S(t, b) at [(t*NSB + b)*BC, +BC) (P aliases its first
 // columns); FP16: O_t (fp32) after all S.  INT8: ACC_t (s32 PV accumulator)
@@ -70,6 +70,11 @@ using namespace sm100;
 
 constexpr int BM = 128;  // query rows per tile (= TMEM lanes)
 constexpr int kMaxPeers = 7;  // output replicas on other GPUs (8 GPUs of one node)
+
+// Tensor maps of the peers' outputs (PeerMaps::m[i] for i < Params::n_peer).
+struct PeerMaps {
+    CUtensorMap m[kMaxPeers];
+};
 
 struct Params {
     int B, H, Hkv, S, KS;
@@ -106,10 +111,8 @@ struct Params {
     int dbg_withhold;
     unsigned long long dbg_wait_limit_ns;
     // output replicas: n_peer other GPUs' counterparts of O (same strides, mapped
-    // into this process), written with the same values as O
+    // into this process; their tensor maps in PeerMaps), written with the same values as O
     int n_peer;
-    __half* o_peer[kMaxPeers];
-    int64_t o_sb, o_sh, o_ss;  // O element strides (batch, head, row)
 };
 
 constexpr int KV_BCAST_KB = 1, KV_BCAST_KH = 2, KV_BCAST_VB = 4, KV_BCAST_VH = 8;
@@ -429,35 +432,6 @@ __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
     return off ^ (((off >> 7) & (SW / 16 - 1)) << 4);
 }
 
-// Copies a tile's staged O (fp16 rows in swizzled boxes, `rows` valid rows of
-// `dv` columns from column dv0) to the same place in each peer's output: 16-byte
-// P2P stores, consecutive threads on consecutive chunks of a row (the rows of a
-// tile are contiguous in a [B, H, S, D] output, so a warp's stores cover 512
-// contiguous bytes).  No fence: the stores are complete when the kernel is, and
-// the peers read them only after that (a collective ordered after this kernel
-// on its stream), so the CTA exits while its stores still drain over NVLink.
-// Not inlined: its registers then do not add to the softmax role's allocation.
-template <class T>
-__device__ __noinline__ void store_peers(const Params& p, const uint8_t* stage, int b, int head, int row0,
-                                            int dv0, int dv, int r) {
-    const int cpr = dv / 8;  // 16-byte chunks per row
-    const int rows = min(BM, p.S - row0);
-    const int64_t base = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(head) * p.o_sh +
-                         static_cast<int64_t>(row0) * p.o_ss + dv0;
-#pragma unroll 1
-    for (int idx = r; idx < rows * cpr; idx += 4 * 32) {
-        const int row = idx / cpr, col = (idx % cpr) * 8;
-        const uint4 v = *reinterpret_cast<const uint4*>(stage + (col / T::O_BOX) * T::O_BOX_BYTES +
-                                                        swz_off<T::O_SW>(row, (col % T::O_BOX) / 8));
-        const int64_t off = base + static_cast<int64_t>(row) * p.o_ss + col;
-        // constant indices: the pointers stay in the parameter bank (a runtime index
-        // would copy the array to local memory)
-#pragma unroll
-        for (int k = 0; k < kMaxPeers; ++k)
-            if (k < p.n_peer) *reinterpret_cast<uint4*>(p.o_peer[k] + off) = v;
-    }
-}
-
 // --------------------------------------------------------------- softmax
 template <class T>
 __device__ __forceinline__ void load_s_row(uint32_t taddr, uint32_t* r) {
@@ -560,7 +534,7 @@ __device__ __forceinline__ bool rotate_q_tiles(const Params& p, const Work& w, u
 // __syncthreads.
 template <class T>
 __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uint8_t* smem, uint32_t tmem,
-                             const Abort& ab) {
+                             const Abort& ab, const PeerMaps* pm) {
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int wq = warp % 4;
@@ -961,15 +935,19 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
         if (lane == 0) mbar_arrive(bar(Bars::O_EMPTY + t));
     }
     mbar_arrive(bar(Bars::EPI + t));
-    if constexpr (!T::DUMP_S) {  // (debug score dumps take no output replicas)
-        if (p.n_peer > 0 && !aborted && warp_wait(bar(Bars::EPI + t), n_st & 1, ab, SITE_SM_EPI) && !*ab.flag)
-            store_peers<T>(p, stage, w.b, w.head[t], row0, dv0, dv, r);
-    }
     if (r == 0) {
         if (!aborted && mbar_wait(bar(Bars::EPI + t), n_st & 1, ab, SITE_SM_EPI) && !*ab.flag) {
             const int nbox = dv / T::O_BOX;
             for (int bx = 0; bx < nbox; ++bx)
                 tma_store_4d(tmO, smem_u32(stage + bx * T::O_BOX_BYTES), dv0 + bx * T::O_BOX, row0, w.head[t], w.b);
+            if constexpr (!T::DUMP_S) {  // (debug score dumps take no output replicas)
+                // the same boxes into every peer's output: the TMA engine carries them
+                // over NVLink while this CTA exits and the next one computes
+                for (int k = 0; k < p.n_peer; ++k)
+                    for (int bx = 0; bx < nbox; ++bx)
+                        tma_store_4d(&pm->m[k], smem_u32(stage + bx * T::O_BOX_BYTES), dv0 + bx * T::O_BOX, row0,
+                                     w.head[t], w.b);
+            }
             bulk_commit();
             // FP16 stages O in Q's buffer: wait here; INT8 waits before the exit
             if constexpr (!T::OWN_STAGE) bulk_wait_read_all();
@@ -980,7 +958,9 @@ __device__ void softmax_role(const Params& p, const CUtensorMap* tmO, int t, uin
     ++n_st;
     }  // items
     if constexpr (T::OWN_STAGE) {
-        if (r == 0) bulk_wait_all();  // the last store has landed before the CTA exits
+        // the stores have read the staging buffer before the CTA (and its shared
+        // memory) goes; their writes complete before the kernel does
+        if (r == 0) bulk_wait_read_all();
     }
 }
 
@@ -1360,7 +1340,7 @@ __device__ void mma_role(const Params& p, uint8_t* smem, uint32_t tmem, const Ab
 // is never rescaled and O = ACC * v_scale / 127 / l at the end.
 template <class T>
 __device__ void softmax_role_i8x2(const Params& p, const CUtensorMap* tmO, int t, uint8_t* smem, uint32_t tmem,
-                                  const Abort& ab) {
+                                  const Abort& ab, const PeerMaps* pm) {
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int wq = warp % 4;
@@ -1566,18 +1546,22 @@ __device__ void softmax_role_i8x2(const Params& p, const CUtensorMap* tmO, int t
         fence_proxy_async_smem();
     }
     mbar_arrive(bar(Bars::EPI + t));
-    if constexpr (!T::DUMP_S) {  // (debug score dumps take no output replicas)
-        if (p.n_peer > 0 && !aborted && warp_wait(bar(Bars::EPI + t), 0, ab, SITE_SM_EPI) && !*ab.flag)
-            store_peers<T>(p, stage, w.b, w.head[t], row0, dv0, dv, r);
-    }
     if (r == 0) {
         if (!aborted && mbar_wait(bar(Bars::EPI + t), 0, ab, SITE_SM_EPI) && !*ab.flag) {
             const int nbox = dv / T::O_BOX;
             for (int bx = 0; bx < nbox; ++bx)
                 tma_store_4d(tmO, smem_u32(stage + bx * T::O_BOX_BYTES), dv0 + bx * T::O_BOX, row0, w.head[t], w.b);
+            if constexpr (!T::DUMP_S) {  // (debug score dumps take no output replicas)
+                // the same boxes into every peer's output: the TMA engine carries them
+                // over NVLink while this CTA exits and the next one computes
+                for (int k = 0; k < p.n_peer; ++k)
+                    for (int bx = 0; bx < nbox; ++bx)
+                        tma_store_4d(&pm->m[k], smem_u32(stage + bx * T::O_BOX_BYTES), dv0 + bx * T::O_BOX, row0,
+                                     w.head[t], w.b);
+            }
             bulk_commit();
         }
-        bulk_wait_all();  // the store has landed before the CTA exits
+        bulk_wait_read_all();  // the stores have read the staging buffer before the CTA exits
     }
 }
 
@@ -1661,7 +1645,7 @@ template <class T>
 __global__ void __launch_bounds__(T::THREADS, T::MIN_BLOCKS)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                      const __grid_constant__ Params p) {
+                      const __grid_constant__ PeerMaps pm, const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x / 32;
@@ -1721,9 +1705,9 @@ __global__ void __launch_bounds__(T::THREADS, T::MIN_BLOCKS)
     }
     if (warp < 4 * T::NT) {
         if constexpr (T::TWOPASS)
-            softmax_role_i8x2<T>(p, &tmO, warp / 4, smem, tmem, ab);
+            softmax_role_i8x2<T>(p, &tmO, warp / 4, smem, tmem, ab, &pm);
         else
-            softmax_role<T>(p, &tmO, warp / 4, smem, tmem, ab);
+            softmax_role<T>(p, &tmO, warp / 4, smem, tmem, ab, &pm);
         tc_fence_before();
     } else if (warp == T::WARP_PROD) {
         if (sm100::lane_id() == 0) producer_kv_role<T>(p, &tmK, &tmV, smem, ab);

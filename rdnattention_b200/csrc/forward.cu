@@ -215,11 +215,14 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
     p.dbg_withhold = g_dbg_withhold;
     p.dbg_wait_limit_ns = g_dbg_wait_limit_ns;
     p.n_peer = g_peers.n;
-    for (int i = 0; i < g_peers.n; ++i) p.o_peer[i] = static_cast<__half*>(g_peers.o[i]);
-    p.o_sb = c.os[0];
-    p.o_sh = c.os[1];
-    p.o_ss = c.os[2];
     const View4 vo{c.o, {c.D, c.S, c.H, c.B}, {c.os[2], c.os[1], c.os[0]}};
+    // the peers' outputs: the same view at each peer's counterpart of c.o
+    PeerMaps pm{};
+    for (int i = 0; i < g_peers.n; ++i) {
+        const View4 vp{g_peers.o[i], {c.D, c.S, c.H, c.B}, {c.os[2], c.os[1], c.os[0]}};
+        if (const char* pe = make_map(&pm.m[i], vp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, T::O_BOX, BM, osw))
+            return fail(err, "%s", pe);
+    }
     const char* e = nullptr;
     if ((e = make_map(&tmQ, vq, dt, T::ESZ, T::BOX, BM, sw)) ||
         (e = make_map(&tmK, vk, dt, T::ESZ, T::BOX, T::BC, sw)) ||
@@ -287,7 +290,7 @@ int launch_prefill(char* err, const Common& c, prefill::Params p, cudaStream_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    ce = launch_timed(stream, [&] { return cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, tmO, p); });
+    ce = launch_timed(stream, [&] { return cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, tmO, pm, p); });
     if (ce == cudaSuccess) ce = cudaGetLastError();
     if (ce != cudaSuccess) return fail(err, "%s", cudaGetErrorString(ce));
     return 0;
