@@ -241,7 +241,7 @@ def test_int8_kv_stride_zero_broadcast():
 @pytest.mark.parametrize("D", [64, 128])
 def test_long_keys_take_the_fold_kernel(D):
     """More than 131072 keys (where 127 * 128 * keys could pass the s32 range) run the
-    one-pass kernel whose correction warpgroup folds the accumulator into an fp32 O:
+    one-pass kernel, whose softmax warps fold the s32 accumulator into an fp32 O:
     flat scores over the first 131072 keys with V at +-127 (its accumulator bound forces
     a fold every few blocks), then a row-max jump of 3 in the exp2 domain (a rescaling
     fold), against the oracle as in test_flat_prefix_then_max_jump; plus random per-token

@@ -83,7 +83,8 @@ def test_fp16_expired_wait_unwinds_and_next_call_is_correct(D, causal):
 
 @pytest.mark.parametrize("D", [64, 128])
 def test_int8_expired_wait_unwinds_and_next_call_is_correct(D):
-    """The INT8 kernels also run the correction warpgroup, whose waits must unwind too."""
+    """The INT8 kernels (one-pass at head_dim 64, two-pass at 128: their own MMA issuer
+    and softmax roles, key-scale hand-off and accumulator folds) unwind the same way."""
     B, H, Hkv, S = 1, 4, 4, 512
     qi, ki, vi, qs, ks, vs, qvec, kvec = gate_i8_inputs(B, H, Hkv, S, S, D, True)
     args = (qi.cuda(), ki.cuda(), vi.cuda(), qvec.cuda(), kvec.cuda(), vs)
