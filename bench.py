@@ -743,6 +743,7 @@ def main():
     scale = 1e9 if cfg["kind"] == "decode" else 1e12
     compute = None
     sym = None
+    gather_used = args.gather if dist_on else None
     if not dist_on:
         fns = [step_fn(cfg, xi) for xi in xs]
         turn = itertools.cycle(fns)
@@ -750,10 +751,13 @@ def main():
         shard = None
     else:
         if args.gather == "fused":
-            from rdnattention_b200.multigpu import SymmetricOutput
+            from rdnattention_b200.multigpu import SymmetricOutput, SymmetricOutputUnavailable
 
-            sym = SymmetricOutput((cfg["B"], cfg["H"], cfg["S"], cfg["D"]))
-            n_pieces = 1
+            try:
+                sym = SymmetricOutput((cfg["B"], cfg["H"], cfg["S"], cfg["D"]))
+                n_pieces = 1
+            except SymmetricOutputUnavailable as ex:  # raised on every rank alike
+                gather_used = f"nccl (the fused gather was unavailable: {str(ex)[:200]})"
         trip = [sharded_step_fns(cfg, xi, world, rank, n_pieces, sym) for xi in xs]
         shard = trip[0][2]
         turn = itertools.cycle([t[0] for t in trip])
@@ -849,13 +853,14 @@ def main():
         "e2e": e2e,
         # (fused gather: the attention launch(es) plus the barrier kernel per step)
         "gpu_launches": args.steps * (launches_per_step(cfg) * (n_pieces if dist_on else 1)
-                                      + (1 if dist_on and args.gather == "fused" else 0)),
+                                      + (1 if sym is not None else 0)),
         "roofline": roof,
         "kernel_status": list(status),
     }
     if compute:
         line["compute_only"] = compute
-        if args.gather == "fused":
+        line["gather"] = gather_used
+        if sym is not None:
             line["step"] = ("flash_attn_sharded(out=SymmetricOutput): one launch per rank computes its units and "
                             "stores every O tile into all ranks' outputs over NVLink (peer stores from the kernel "
                             "epilogue), then a barrier kernel (epoch flags written over NVLink) orders the stores")

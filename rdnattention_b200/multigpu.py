@@ -159,6 +159,10 @@ def auto_chunks(batch: int, heads: int, seq: int, head_dim: int, world: int, ele
     return 2 if per_batch >= AUTO_PIECE_BYTES and local >= 2 else 1
 
 
+class SymmetricOutputUnavailable(RuntimeError):
+    """Raised on every rank when a SymmetricOutput cannot be set up on some rank."""
+
+
 class _DeviceArray:
     """A raw device allocation seen through __cuda_array_interface__ (torch.as_tensor)."""
 
@@ -174,7 +178,10 @@ class SymmetricOutput:
     all-gather fused into the attention epilogue.
 
     Collective: every rank constructs it with the same shape (on its current
-    CUDA device) and calls close() together.  `slots` buffers are used in turn,
+    CUDA device) and calls close() together.  Construction fails on every rank
+    alike (SymmetricOutputUnavailable, after undoing what succeeded) when any
+    rank cannot allocate or map the buffers, so callers can fall back to the
+    NCCL gather without the ranks' collectives diverging.  `slots` buffers are used in turn,
     one per call: the tensor a call returns holds the result until this rank
     makes its next call with this object (consume or copy it, on the current
     stream, before then); other ranks' next kernels only write the following
@@ -200,25 +207,59 @@ class SymmetricOutput:
             n *= x
         self.slot_bytes = (n * 2 + 255) // 256 * 256
         flags_off = self.slot_bytes * slots  # then one flag word per rank (the barrier's epochs)
-        with torch.cuda.device(self.device):
-            self._base, handle = R._ipc_alloc(flags_off + 256)
-        self._flags = torch.as_tensor(_DeviceArray(self._base + flags_off, (self.world,), "<i4"), device=self.device)
-        self._flags.zero_()  # before the handles go out: no peer signals before it has them
+        self._base = None
+        self._peer_bases = []  # the other ranks' allocations, in rank order
+        handle, why = bytes(R.IPC_HANDLE_BYTES), None
+        try:
+            with torch.cuda.device(self.device):
+                self._base, handle = R._ipc_alloc(flags_off + 256)
+            self._flags = torch.as_tensor(_DeviceArray(self._base + flags_off, (self.world,), "<i4"),
+                                          device=self.device)
+            self._flags.zero_()  # before the handles go out: no peer signals before it has them
+        except Exception as ex:  # noqa: BLE001 - reported collectively below
+            why = f"allocation failed on rank {self.rank}: {ex}"
         self._epoch = 0
+        # every rank takes part in the exchange, whether or not its allocation succeeded
         mine = torch.frombuffer(bytearray(handle), dtype=torch.uint8).to(self.device)
         every = torch.empty(self.world * R.IPC_HANDLE_BYTES, dtype=torch.uint8, device=self.device)
         dist.all_gather_into_tensor(every, mine, group=group)
+        self._agree(why)
         every = every.cpu().numpy().tobytes()
-        self._peer_bases = []  # the other ranks' allocations, in rank order
-        with torch.cuda.device(self.device):
-            for r in range(self.world):
-                if r != self.rank:
-                    h = every[r * R.IPC_HANDLE_BYTES:(r + 1) * R.IPC_HANDLE_BYTES]
-                    self._peer_bases.append(R._ipc_open(h))
+        try:
+            with torch.cuda.device(self.device):
+                for r in range(self.world):
+                    if r != self.rank:
+                        h = every[r * R.IPC_HANDLE_BYTES:(r + 1) * R.IPC_HANDLE_BYTES]
+                        self._peer_bases.append(R._ipc_open(h))
+        except Exception as ex:  # noqa: BLE001 - reported collectively below
+            why = f"mapping a peer's buffer failed on rank {self.rank}: {ex}"
+        self._agree(why)
         self._peer_flags = [b + flags_off for b in self._peer_bases]
         self.slots = [torch.as_tensor(_DeviceArray(self._base + i * self.slot_bytes, self.shape, "<f2"),
                                       device=self.device) for i in range(slots)]
         self._turn = 0
+
+    def _agree(self, why):
+        """Collective success check: if any rank failed, every rank undoes what it
+        holds and raises SymmetricOutputUnavailable (the failing ranks' reasons)."""
+        import rdnattention_b200 as R
+
+        ok = torch.tensor([0 if why else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if int(ok.item()) == 1:
+            return
+        reasons = [None] * self.world
+        dist.all_gather_object(reasons, why, group=self.group)
+        for b in self._peer_bases:
+            with torch.cuda.device(self.device):
+                R._ipc_close(b)
+        self._peer_bases = []
+        dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
+        if self._base is not None:
+            with torch.cuda.device(self.device):
+                R._ipc_free(self._base)
+            self._base = None
+        raise SymmetricOutputUnavailable("; ".join(r for r in reasons if r))
 
     def next_slot(self):
         """The slot the next call writes, and its offset in every allocation."""

@@ -10,7 +10,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from rdnattention_b200.multigpu import SymmetricOutput, _uniform_axis, flash_attn_sharded, local_views, pieces, plan
+from rdnattention_b200.multigpu import (SymmetricOutput, SymmetricOutputUnavailable, _uniform_axis, flash_attn_sharded,
+                                        local_views, pieces, plan)
 
 
 @pytest.mark.parametrize("B,Hkv,world", [(4, 8, 2), (1, 8, 2), (3, 2, 2), (1, 1, 2), (8, 8, 8), (2, 3, 4), (5, 8, 8),
@@ -234,3 +235,43 @@ def test_int8_sharded_slices_the_per_token_scales(shape, world, chunks):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert results == {r: True for r in range(world)}
+
+
+def _agree_worker(rank, world, port, failing, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        so = SymmetricOutput.__new__(SymmetricOutput)
+        so.group, so.world, so.rank = None, world, rank
+        so.device = torch.device("cpu")
+        so._base, so._peer_bases = None, []
+        why = f"no IPC here (rank {rank})" if rank in failing else None
+        try:
+            so._agree(why)
+            queue.put((rank, "ok"))
+        except SymmetricOutputUnavailable as ex:
+            queue.put((rank, str(ex)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("failing", [(), (1,), (0, 2)])
+def test_symmetric_output_fails_on_every_rank_alike(failing):
+    """A SymmetricOutput that cannot be set up on one rank fails on all of them,
+    with every failing rank's reason, so the ranks' collectives never diverge."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_agree_worker, args=(r, world, port, failing, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    if not failing:
+        assert set(results.values()) == {"ok"}
+    else:
+        want = "; ".join(f"no IPC here (rank {r})" for r in failing)
+        assert all(v == want for v in results.values()), results
