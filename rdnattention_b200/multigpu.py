@@ -7,7 +7,8 @@ units and every rank receives the full output O.  Two ways to assemble O:
 * fused (``out=SymmetricOutput(...)``): every rank's output buffer is mapped
   into every other rank's process (CUDA IPC), and the attention kernels store
   each finished O tile into all ranks' buffers over NVLink from their
-  epilogue, so the gather overlaps the tiles still being computed; a small
+  epilogue (TMA stores, one tensor map per peer), so the gather overlaps the
+  tiles still being computed; a small
   barrier kernel (epoch flags written over NVLink) then orders the peers'
   stores before anything that reads O;
 * NCCL: the rank's units are computed into its block of O and NCCL
@@ -311,8 +312,10 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
                        out: Optional[SymmetricOutput] = None, q_side=None, kv_side=None):
     """Forward attention over all ranks of `group`: every rank passes the same full
     [B, H, S, D] / [B, Hkv, KS, D] inputs, computes only its (batch, KV-head) units
-    and receives the full output.  `compute` replaces the local kernel call
-    (default: the sm_100a path through the C ABI).
+    and receives the full output.  `compute(q, k, v, out=..., is_causal=...,
+    window_size=..., rot_cos=..., rot_sin=...)` replaces the local kernel call
+    (default: the sm_100a path through the C ABI); with `out` it also receives
+    `peer_outputs`, and `q_side` / `kv_side` when given.
 
     When the plan splits one axis evenly (the usual case), each rank writes its
     units straight into its block of the result and the all-gathers run in place
@@ -323,9 +326,10 @@ def flash_attn_sharded(query, key, value, is_causal: bool = False, window_size: 
     c + 1 (a batch split is then round robin, and a piece holding several batch
     elements of it is gathered through a staging buffer in one collective).  With
     one piece a batch split takes consecutive ranges and a single in-place
-    all-gather.  chunks=None picks the count from O's size (auto_chunks).  Uneven plans gather pieces into a staging buffer and copy them
-    into place; every rank takes the same collective steps (pieces that are empty
-    on some ranks are padded).
+    all-gather.  chunks=None picks the count from O's size (auto_chunks).
+    Uneven plans gather pieces into a staging buffer and copy them into place;
+    every rank takes the same collective steps (pieces that are empty on some
+    ranks are padded).
 
     With `out` (a SymmetricOutput of O's shape on `group`) the gather is fused
     into the kernels: one launch computes the rank's units and stores every O
