@@ -507,6 +507,24 @@ def load_peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
+def tensor_peak(kind, clocks):
+    """(peak, burst, sustained, source, regime) of the tensor roofline: the measured
+    burst figure for a short timed region, the sustained one when NVML reported
+    sw_power_cap during it (the regime the sustained figure was measured in)."""
+    peak_tc, peak_tc_sus, _, peak_src = load_peaks()
+    if kind == "int8":
+        burst, sus = load_int8_peak("burst"), load_int8_peak("sustained")
+        src = "measured (profiles/int8_peak.txt, torch._int_mm)"
+        if burst is None or sus is None:
+            burst, sus, src = 2 * peak_tc, 2 * peak_tc_sus, f"{peak_src} (MEASURED_PEAKS.json bf16 x2)"
+    else:
+        burst, sus, src = peak_tc, peak_tc_sus, f"{peak_src} (MEASURED_PEAKS.json bf16)"
+    capped = "sw_power_cap" in (clocks.get("reasons") or [])
+    regime = ("sustained (sw_power_cap active during the timed region)" if capped
+              else "burst (no power cap during the timed region)")
+    return (sus if capped else burst), burst, sus, src, regime
+
+
 # Nominal dense peaks of one B200 (spec sheet), reported beside the measured ones.
 SPEC_PEAKS = {"fp16": 2250.0, "int8": 4500.0, "hbm": 8000.0}
 
@@ -807,30 +825,20 @@ def main():
         return
 
     metric, unit = metric_of(cfg)
-    peak_tc, peak_tc_sus, peak_hbm, peak_src = load_peaks()
+    _, _, peak_hbm, peak_src = load_peaks()
     # the roofline is the per-GPU attention kernel's (at N > 1 on the rank's own units)
     k_ms = kernel_ms
     k_units = per_step_units * (compute["units_per_rank_max"] / (cfg["B"] * cfg["Hkv"]) if compute else 1.0)
     clocks = sampler.summary()
-    # Tensor peaks: the burst figure for a short timed region, the sustained one when
-    # the 1 kW power cap engaged during it (the regime the sustained GEMM was measured in)
-    capped = "sw_power_cap" in (clocks.get("reasons") or [])
     if cfg["kind"] == "decode":
         roof = {"bound": "hbm", "achieved": k_units / (k_ms / 1e3) / 1e9, "peak": peak_hbm, "unit": "GB/s"}
         roof["peak_source"] = f"{peak_src} (MEASURED_PEAKS.json copy)"
     else:
-        if cfg["kind"] == "int8":
-            burst, sus = load_int8_peak("burst"), load_int8_peak("sustained")
-            src = "measured (profiles/int8_peak.txt, torch._int_mm)"
-            if burst is None:
-                burst, sus, src = 2 * peak_tc, 2 * peak_tc_sus, f"{peak_src} (MEASURED_PEAKS.json bf16 x2)"
-        else:
-            burst, sus, src = peak_tc, peak_tc_sus, f"{peak_src} (MEASURED_PEAKS.json bf16)"
+        peak, burst, sus, src, regime = tensor_peak(cfg["kind"], clocks)
         achieved = k_units / (k_ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": sus if capped else burst,
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TOP/s" if cfg["kind"] == "int8" else "TFLOP/s"}
-        roof["peak_regime"] = ("sustained (sw_power_cap active during the timed region)" if capped
-                               else "burst (no power cap during the timed region)")
+        roof["peak_regime"] = regime
         roof["frac_of_burst"] = achieved / burst
         roof["frac_of_sustained"] = achieved / sus
         roof["peak_source"] = src

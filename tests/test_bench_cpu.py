@@ -51,3 +51,14 @@ def test_help_and_work_units():
     dec = bench.CONFIGS["5"]
     kv = 2 * dec["B"] * dec["Hkv"] * dec["KS"] * dec["D"] * 2
     assert bench.work_units(dec) >= kv
+
+
+def test_tensor_peak_follows_the_power_regime():
+    """The roofline divides by the burst peak unless the power cap engaged during the
+    timed region, then by the sustained one; INT8 uses the int8 peaks it measured."""
+    peak, burst, sus, _, regime = bench.tensor_peak("fp16", {"reasons": []})
+    assert peak == burst and sus <= burst and regime.startswith("burst")
+    peak, burst, sus, _, regime = bench.tensor_peak("fp16", {"reasons": ["sw_power_cap"]})
+    assert peak == sus and regime.startswith("sustained")
+    peak8, burst8, sus8, src8, _ = bench.tensor_peak("int8", {"reasons": []})
+    assert peak8 == burst8 and burst8 > burst and sus8 < burst8
