@@ -275,3 +275,33 @@ def test_symmetric_output_fails_on_every_rank_alike(failing):
     else:
         want = "; ".join(f"no IPC here (rank {r})" for r in failing)
         assert all(v == want for v in results.values()), results
+
+
+def test_sharded_argument_checks_and_single_rank():
+    """One-rank group (gloo, in this process): a SymmetricOutput of the wrong shape and
+    chunks < 1 are rejected before any work, and a single rank computes everything."""
+    from oracle import torch_oracle
+
+    store = dist.TCPStore("127.0.0.1", _free_port(), 1, True)
+    dist.init_process_group("gloo", store=store, rank=0, world_size=1)
+    try:
+        g = torch.Generator().manual_seed(3)
+        q = torch.randn(2, 4, 9, 32, generator=g).half()
+        k = torch.randn(2, 2, 9, 32, generator=g).half()
+
+        def compute(qs, ks, vs, out=None, **kw):
+            o = torch_oracle.attention(qs, ks, vs, causal=kw["is_causal"], window=kw["window_size"]).half()
+            if out is not None:
+                out.copy_(o)
+            return o
+
+        wrong = SymmetricOutput.__new__(SymmetricOutput)
+        wrong.shape, wrong.world, wrong.rank = (2, 4, 9, 16), 1, 0
+        with pytest.raises(ValueError):
+            flash_attn_sharded(q, k, k, compute=compute, out=wrong)
+        with pytest.raises(ValueError):
+            flash_attn_sharded(q, k, k, compute=compute, chunks=0)
+        got = flash_attn_sharded(q, k, k, is_causal=True, compute=compute)
+        assert torch.equal(got, torch_oracle.attention(q, k, k, causal=True).half())
+    finally:
+        dist.destroy_process_group()
